@@ -1,0 +1,663 @@
+"""Benchmark of the redistribute collectives (BASELINE.json metric: redistribute bus GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--op OP] [--sweep]
+
+N = 1: the reference's same-device mode -- every rank of the group on one GPU, one kernel does the whole
+       collective (HBM-bound: the rank-order reduce reads n partials and writes one result).
+N > 1: launched by torchrun, one process per GPU; each process is one rank of a dt_comm whose peers are
+       IPC-mapped, and the kernels move data through peer HBM over NVLink.
+
+The default workload is BASELINE configs[1]: all-reduce Partial->Replicate, bf16 (8192, 8192), rank r's
+partial N(0,1) from seed + r, fp32 accumulation in rank order. `--op` selects the other configs.
+
+`value` is the whole-job aggregate bus bandwidth: the nccl-tests bus bandwidth of one rank (algorithm
+bandwidth times 2(n-1)/n for all-reduce, (n-1)/n for the others) times the number of GPUs. `bus_gbs_per_rank`
+is the per-rank figure and `pct_nvlink_peak` compares it with 900 GB/s per direction.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+os.environ.setdefault("DTORCH_COMM_TIMEOUT_SECOND", "60")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+NVLINK_NOMINAL_GBS = 900.0      # NVLink 5, per direction per GPU
+NVLINK_PEER_COPY_GBS = 770.0    # measured peer copy per direction on this pool (profiling recipe)
+FALLBACK_HBM_GBS = 6650.0
+
+# ---------------------------------------------------------------------------------------------------------
+# Workloads
+# ---------------------------------------------------------------------------------------------------------
+CONFIGS = {
+    "all_gather": dict(name="C1 all-gather Shard(0)->Replicate fp32 (4096,4096)", dtype=torch.float32,
+                       global_shape=(4096, 4096), dist="rand", emul_n=2),
+    "all_reduce": dict(name="C2 all-reduce Partial->Replicate bf16 (8192,8192)", dtype=torch.bfloat16,
+                       shape=(8192, 8192), dist="randn", emul_n=8),
+    "reduce_scatter": dict(name="C3 reduce-scatter Partial->Shard(0) bf16 (16384,8192)", dtype=torch.bfloat16,
+                           shape=(16384, 8192), dist="randn", emul_n=8),
+    "all_to_all": dict(name="C4 Ulysses all-to-all Shard(1)->Shard(2) bf16 (1,65536,64,128)", dtype=torch.bfloat16,
+                       global_shape=(1, 65536, 64, 128), dist="randn", emul_n=8, src_dim=1, dst_dim=2),
+}
+DT_NAME = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}
+
+
+def shard_sizes(length, n):
+    return [length // n + (1 if i < length % n else 0) for i in range(n)]
+
+
+def bus_factor(op, n):
+    return 2.0 * (n - 1) / n if op == "all_reduce" else (n - 1) / n
+
+
+def gen(shape, dtype, seed, dist, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    if dist == "rand":
+        t = torch.rand(*shape, generator=g, device=device)
+    elif dist == "uniform":
+        t = torch.rand(*shape, generator=g, device=device) * 2 - 1
+    else:
+        t = torch.randn(*shape, generator=g, device=device)
+    return t.to(dtype)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
+
+
+def profile_traffic(key):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML; nvidia-smi as fallback)
+# ---------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.dev = device_index
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.nv = None
+
+    def _sample(self):
+        nv = self.nv
+        mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        self.samples.append(mhz)
+        self.reasons |= int(r)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+            if not self.samples:
+                try:
+                    self._sample()
+                except Exception:
+                    pass
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        names = [k for k, v in self.REASONS.items() if self.reasons & v and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------------------
+# 1-GPU (same-device) workloads
+# ---------------------------------------------------------------------------------------------------------
+class LocalWorkload:
+    """n emulated ranks on cuda:0; one same-device kernel per step."""
+
+    def __init__(self, op, cfg, stream):
+        from dtorch_b200 import capi
+
+        self.capi = capi
+        self.op = op
+        self.cfg = cfg
+        self.n = cfg["emul_n"]
+        self.stream = stream
+        self.dtype = cfg["dtype"]
+        self.es = torch.tensor([], dtype=self.dtype).element_size()
+        dev = "cuda:0"
+        n = self.n
+        if op in ("all_reduce", "reduce_scatter"):
+            self.ins = [gen(cfg["shape"], self.dtype, r, cfg["dist"], dev).reshape(-1) for r in range(n)]
+            self.msg_bytes = self.ins[0].numel() * self.es  # per-rank buffer (AR) / per-rank input (RS)
+            if op == "all_reduce":
+                self.outs = [torch.empty_like(self.ins[0])]
+            else:
+                self.outs = [torch.empty(self.ins[0].numel() // n, dtype=self.dtype, device=dev) for _ in range(n)]
+            self.hbm_bytes = (n + 1) * self.msg_bytes if op == "all_reduce" else (n + 1) * self.msg_bytes // 1
+            if op == "reduce_scatter":
+                self.hbm_bytes = n * self.msg_bytes + self.msg_bytes  # read n inputs, write n chunks of S/n
+        elif op == "all_gather":
+            gs = cfg["global_shape"]
+            lens = shard_sizes(gs[0], n)
+            full = gen(gs, self.dtype, 0, cfg["dist"], dev)
+            self.ins = [t.contiguous() for t in torch.split(full, lens, 0)]
+            self.lens = lens
+            self.inner = int(np.prod(gs[1:])) * self.es
+            self.outs = [torch.empty(gs, dtype=self.dtype, device=dev)]
+            self.msg_bytes = full.numel() * self.es  # S = output size
+            self.hbm_bytes = 2 * self.msg_bytes
+        else:  # all_to_all
+            gs = list(cfg["global_shape"])
+            sd, dd = cfg["src_dim"], cfg["dst_dim"]
+            full = gen(gs, self.dtype, 0, cfg["dist"], dev)
+            self.src_lens = shard_sizes(gs[sd], n)
+            self.ins = [t.contiguous() for t in torch.split(full, self.src_lens, sd)]
+            split = shard_sizes(gs[dd], n)
+            self.outs = []
+            for k in range(n):
+                shp = list(gs)
+                shp[dd] = split[k]
+                self.outs.append(torch.empty(shp, dtype=self.dtype, device=dev))
+            self.in_shape = list(self.ins[0].shape)
+            self.msg_bytes = self.ins[0].numel() * self.es  # per-rank buffer
+            self.hbm_bytes = 2 * full.numel() * self.es
+        self.in_ptrs = [t.data_ptr() for t in self.ins]
+        self.out_ptrs = [t.data_ptr() for t in self.outs]
+        # pinned host copies for the end-to-end leg
+        self.h_ins = [t.cpu().pin_memory() for t in self.ins]
+        self.h_outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in self.outs]
+        self.h2d = sum(t.numel() * self.es for t in self.ins)
+        self.d2h = sum(t.numel() * self.es for t in self.outs)
+
+    def step(self):
+        c = self.capi
+        s = self.stream.cuda_stream
+        if self.op == "all_reduce":
+            code = c.dtype_code(self.dtype)
+            c.local_all_reduce(self.in_ptrs, self.out_ptrs[0], self.ins[0].numel(), code, 0, s)
+        elif self.op == "reduce_scatter":
+            code = c.dtype_code(self.dtype)
+            c.local_reduce_scatter(self.in_ptrs, self.out_ptrs, self.outs[0].numel(), code, 0, s)
+        elif self.op == "all_gather":
+            c.local_all_gather(self.in_ptrs, self.out_ptrs[0], 1, self.lens, self.inner, s)
+        else:
+            c.local_all_to_all(self.in_ptrs, self.out_ptrs, self.in_shape, self.cfg["src_dim"], self.cfg["dst_dim"],
+                               self.src_lens, self.es, s)
+
+    def e2e_step(self):
+        with torch.cuda.stream(self.stream):
+            for d, h in zip(self.ins, self.h_ins):
+                d.copy_(h, non_blocking=True)
+            self.step()
+            for h, d in zip(self.h_outs, self.outs):
+                h.copy_(d, non_blocking=True)
+
+
+def time_steps(fn, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps  # ms per step
+
+
+# ---------------------------------------------------------------------------------------------------------
+# CPU baseline: the reference's own thread-group code (oracle/_ref) on this host's cores
+# ---------------------------------------------------------------------------------------------------------
+def cpu_inputs(op, cfg, n):
+    """Seeded host inputs of the workload as raw numpy storage (uint16 bits for bf16). Generated on the GPU
+    when one is present (much faster than the CPU generator), then copied to host memory."""
+    dtype = cfg["dtype"]
+    gdev = "cuda" if torch.cuda.is_available() else "cpu"
+
+    def raw(t):
+        t = t.contiguous()
+        return t.numpy() if t.dtype == torch.float32 else t.view(torch.int16).numpy().view(np.uint16)
+
+    if op in ("all_reduce", "reduce_scatter"):
+        return [raw(gen(cfg["shape"], dtype, r, cfg["dist"], gdev).reshape(-1).cpu()) for r in range(n)]
+    gs = cfg["global_shape"]
+    full = gen(gs, dtype, 0, cfg["dist"], gdev).cpu()
+    dim = 0 if op == "all_gather" else cfg["src_dim"]
+    return [raw(t) for t in torch.split(full, shard_sizes(gs[dim], n), dim)]
+
+
+def sample_inputs(op, cfg, ins, frac):
+    """A leading fraction of the workload with the same layout (rows of dim 0 of the global tensor)."""
+    if frac >= 1.0:
+        return ins
+    n = len(ins)
+    if op in ("all_reduce", "reduce_scatter"):
+        m = max(n, int(ins[0].size * frac) // n * n)
+        return [a[:m] for a in ins]
+    if op == "all_gather":
+        return [a[: max(1, int(a.shape[0] * frac))] for a in ins]
+    # all-to-all: cut the source-dim shards (Ulysses sequence) proportionally
+    sd = cfg["src_dim"]
+    return [np.ascontiguousarray(np.take(a, range(max(1, int(a.shape[sd] * frac))), axis=sd)) for a in ins]
+
+
+def cpu_reference_run(op, cfg, ins, reps, threads):
+    """Time the reference's CPU DeviceMesh path on `ins`; returns (per-rep seconds list, kind)."""
+    from oracle.oracle import Reference, Restatement
+
+    code = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[cfg["dtype"]]
+    if Reference.available():
+        ref = Reference()
+        if op == "all_reduce":
+            _, s = ref.all_reduce(ins, code, iters=reps, threads=threads)
+        elif op == "reduce_scatter":
+            _, s = ref.reduce_scatter(ins, code, iters=reps, threads=threads)
+        elif op == "all_gather":
+            _, s = ref.all_gather(ins, code, 0, iters=reps, threads=threads)
+        else:
+            _, s = ref.all_to_all(ins, code, cfg["src_dim"], cfg["dst_dim"], iters=reps, threads=threads)
+        return [float(v) for v in s], "reference"
+    R = Restatement()
+    out = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        if op == "all_reduce":
+            R.fold_sum(ins, code, True)
+        elif op == "reduce_scatter":
+            R.reduce_scatter(ins, code, True)
+        elif op == "all_gather":
+            R.all_gather(ins, 0)
+        else:
+            R.all_to_all(ins, cfg["src_dim"], cfg["dst_dim"])
+        out.append(time.perf_counter() - t0)
+    return out, "port"
+
+
+def msg_bytes_of(op, ins):
+    """Per-rank message size S of the nccl-tests formulas for host inputs `ins`."""
+    if op in ("all_reduce", "reduce_scatter", "all_to_all"):
+        return ins[0].nbytes
+    return sum(a.nbytes for a in ins)  # all-gather: S = output size
+
+
+def cpu_baseline(op, cfg, n, budget_s=20.0):
+    """Bounded CPU baseline: one probe repetition on a sample, then as many repetitions as fit the budget."""
+    cores = os.cpu_count() or 1
+    full = cpu_inputs(op, cfg, n)
+    frac = 1.0
+    ins = full
+    probe, kind = cpu_reference_run(op, cfg, ins, 1, cores)
+    if probe[0] > budget_s / 3:
+        frac = max(1.0 / 64, budget_s / 3 / probe[0])
+        ins = sample_inputs(op, cfg, full, frac)
+    reps = 3
+    secs, kind = cpu_reference_run(op, cfg, ins, reps, cores)
+    t = statistics.median(secs)
+    msg = msg_bytes_of(op, ins)
+    threads = cores if kind == "reference" else 1
+    sample = (f"{'full workload' if frac >= 1 else f'{frac:.3f} of the workload (leading rows)'}, median of {reps} "
+              f"repetitions, n={n} rank threads on a CPU DeviceMesh, torch intra-op threads={threads}, "
+              f"the reference's pre-collective Barrier included" if kind == "reference" else
+              f"C restatement (single thread), {frac:.3f} of the workload")
+    return t, msg, {"kind": kind, "cores": threads, "sample": sample}
+
+
+# ---------------------------------------------------------------------------------------------------------
+# Arms
+# ---------------------------------------------------------------------------------------------------------
+def run_ours_single(args):
+    from dtorch_b200 import capi
+
+    op = args.op
+    cfg = CONFIGS[op]
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream(device=0)
+    w = LocalWorkload(op, cfg, stream)
+    n = w.n
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            w.step()
+    torch.cuda.synchronize()
+    l0 = capi.launch_count()
+    with ClockSampler(0) as clk:
+        with torch.cuda.stream(stream):
+            ms = time_steps(w.step, args.steps, stream)
+    launches = capi.launch_count() - l0
+    # end to end: pinned host -> device, collective, device -> pinned host, every step
+    if args.skip_e2e:
+        e2e_ms = float("nan")
+    else:
+        for _ in range(max(1, args.warmup // 2)):
+            w.e2e_step()
+        torch.cuda.synchronize()
+        e2e_ms = time_steps(w.e2e_step, args.steps, stream)
+    t = ms / 1e3
+    bus = w.msg_bytes * bus_factor(op, n) / t / 1e9
+    e2e_bus = w.msg_bytes * bus_factor(op, n) / (e2e_ms / 1e3) / 1e9
+    peaks, peak_src = measured_peaks()
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    achieved = w.hbm_bytes / t / 1e9
+    # CPU baseline on this host: the reference's own CPU thread-group path, same workload
+    if args.skip_cpu:
+        cpu_t, cpu_msg, cpu_info = float("nan"), w.msg_bytes, {"kind": "skipped", "cores": 0, "sample": "--skip-cpu"}
+    else:
+        cpu_t, cpu_msg, cpu_info = cpu_baseline(op, cfg, n)
+    cpu_bus = cpu_msg * bus_factor(op, n) / cpu_t / 1e9
+    line = {
+        "metric": "redistribute bus GB/s",
+        "value": round(bus, 2),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": DT_NAME[cfg["dtype"]],
+        "data": "synthetic (seeded, BASELINE.json distribution)",
+        "config": {"workload": cfg["name"] + f", same-device group of {n} ranks on 1 GPU (reference same-device "
+                   "mode), one kernel per step", "op": op, "group_ranks": n, "msg_bytes_per_rank": w.msg_bytes,
+                   "accumulate": "fp32, rank order" if op in ("all_reduce", "reduce_scatter") else "copy",
+                   "l2": "inputs larger than L2 (126 MB); no flush", "parallelism": "same-device"},
+        "bus_gbs_per_rank": round(bus, 2),
+        "pct_nvlink_peak": None,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": profile_traffic(f"local_{op}"),
+                     "algorithmic_bytes_per_launch": w.hbm_bytes, "peak_source": f"{peak_src} hbm_gbs"},
+        "cpu_baseline": {"value": round(cpu_bus, 4), "unit": "GB/s", "cores": cpu_info["cores"],
+                         "kind": cpu_info["kind"], "sample": cpu_info["sample"], "seconds_per_op": round(cpu_t, 4)},
+        "e2e": {"value": round(e2e_bus, 3), "unit": "GB/s", "h2d_bytes_per_step": w.h2d, "d2h_bytes_per_step": w.d2h,
+                "ms_per_step": round(e2e_ms, 4), "path": "C ABI (dt_local_*) with pinned host buffers"},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line))
+
+
+def run_reference(args, rank, world):
+    """The reference's own CPU thread-group implementation on this host's cores, same config and metric.
+    Under torchrun only rank 0 runs it (the CPU mesh lives in one process); the other ranks exit."""
+    op = args.op
+    cfg = CONFIGS[op]
+    n = world if world > 1 else cfg["emul_n"]
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    full = cpu_inputs(op, cfg, n)
+    probe, kind = cpu_reference_run(op, cfg, full, 1, cores)
+    # each step is a bounded sample so the whole run stays within a few minutes
+    budget = 150.0
+    frac = min(1.0, max(1.0 / 64, budget / max(1, args.warmup + args.steps) / max(probe[0], 1e-6)))
+    ins = sample_inputs(op, cfg, full, frac)
+    secs, kind = cpu_reference_run(op, cfg, ins, args.warmup + args.steps, cores)
+    t = statistics.median(secs[args.warmup:])
+    msg = msg_bytes_of(op, ins)
+    bus = msg * bus_factor(op, n) / t / 1e9
+    threads = cores if kind == "reference" else 1
+    sample = (f"{'full workload' if frac >= 1 else f'{frac:.3f} of the workload (leading rows)'} per step, "
+              f"n={n} rank threads, torch intra-op threads={threads}")
+    line = {
+        "metric": "redistribute bus GB/s", "value": round(bus, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DT_NAME[cfg["dtype"]],
+        "data": "synthetic (seeded, BASELINE.json distribution)", "impl": "reference",
+        "config": {"workload": cfg["name"] + f", reference CPU DeviceMesh path (ThreadGroupSameDeviceBackend), "
+                   f"group of {n} rank threads", "op": op, "group_ranks": n, "msg_bytes_per_rank": msg},
+        "cpu_baseline": {"value": round(bus, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": round(bus, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+class _CAI:
+    def __init__(self, ptr, numel, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (numel,), "typestr": typestr, "version": 3,
+                                         "strides": None}
+
+
+def heap_tensor(base, offset, numel, dtype, device):
+    ts = {torch.float32: "<f4", torch.bfloat16: "<i2", torch.float16: "<i2"}[dtype]
+    t = torch.as_tensor(_CAI(base + offset, numel, ts), device=device)
+    return t.view(dtype) if dtype != torch.float32 else t
+
+
+def run_ours_multi(args, rank, world, local_rank):
+    """One rank per process; peers IPC-mapped through the communicator's symmetric heap."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from dtorch_b200 import capi
+
+    op = args.op
+    cfg = CONFIGS[op]
+    n = world
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    dtype = cfg["dtype"]
+    es = torch.tensor([], dtype=dtype).element_size()
+    # per-rank buffers
+    if op in ("all_reduce", "reduce_scatter"):
+        in_numel = int(np.prod(cfg["shape"]))
+        out_numel = in_numel if op == "all_reduce" else in_numel // n
+        msg = in_numel * es
+    elif op == "all_gather":
+        gs = cfg["global_shape"]
+        lens = shard_sizes(gs[0], n)
+        inner = int(np.prod(gs[1:]))
+        in_numel = lens[rank] * inner
+        out_numel = gs[0] * inner
+        msg = out_numel * es
+    else:
+        gs = list(cfg["global_shape"])
+        sd, dd = cfg["src_dim"], cfg["dst_dim"]
+        src_lens = shard_sizes(gs[sd], n)
+        split = shard_sizes(gs[dd], n)
+        in_shape = list(gs)
+        in_shape[sd] = src_lens[rank]
+        in_numel = int(np.prod(in_shape))
+        out_numel = int(np.prod(gs)) // gs[sd] * gs[sd] // gs[dd] * split[rank]
+        msg = in_numel * es
+    align = 1 << 20
+    in_bytes = (in_numel * es + align - 1) // align * align
+    out_bytes = (out_numel * es + align - 1) // align * align
+    comm = capi.Comm.for_rank(n, rank, local_rank, in_bytes + out_bytes)
+    handles = [None] * n
+    dist.all_gather_object(handles, comm.export_handle())
+    comm.import_handles(handles)
+    base, _ = comm.heap(rank)
+    x = heap_tensor(base, 0, in_numel, dtype, dev)
+    y = heap_tensor(base, in_bytes, out_numel, dtype, dev)
+    if op in ("all_reduce", "reduce_scatter"):
+        x.copy_(gen(cfg["shape"], dtype, rank, cfg["dist"], dev).reshape(-1))
+    elif op == "all_gather":
+        x.copy_(gen(gs, dtype, 0, cfg["dist"], dev)[sum(lens[:rank]):sum(lens[:rank + 1])].reshape(-1))
+    else:
+        full = gen(gs, dtype, 0, cfg["dist"], dev)
+        x.copy_(torch.split(full, src_lens, sd)[rank].reshape(-1))
+        del full
+    stream = torch.cuda.current_stream(dev)
+    code = capi.dtype_code(dtype) if dtype in (torch.float32, torch.bfloat16, torch.float16) else 0
+
+    def step():
+        s = stream.cuda_stream
+        if op == "all_reduce":
+            comm.all_reduce(rank, x.data_ptr(), y.data_ptr(), in_numel, code, 0, s)
+        elif op == "reduce_scatter":
+            comm.reduce_scatter(rank, x.data_ptr(), y.data_ptr(), out_numel, code, 0, s)
+        elif op == "all_gather":
+            comm.all_gather(rank, x.data_ptr(), y.data_ptr(), 1, lens, inner * es, s)
+        else:
+            comm.all_to_all(rank, x.data_ptr(), y.data_ptr(), in_shape, sd, dd, src_lens, es, s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    l0 = capi.launch_count()
+    with ClockSampler(local_rank) as clk:
+        ms = time_steps(step, args.steps, stream)
+    launches = capi.launch_count() - l0
+    dist.barrier()
+    t_max = torch.tensor([ms], device=dev)
+    dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+    err = comm.error(rank)
+    # end to end: pinned host input -> heap, collective, heap output -> pinned host
+    h_in = x.cpu().pin_memory()
+    h_out = torch.empty(out_numel, dtype=dtype).pin_memory()
+
+    def e2e_step():
+        x.copy_(h_in, non_blocking=True)
+        step()
+        h_out.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = time_steps(e2e_step, args.steps, stream)
+    dist.barrier()
+    t_max = torch.tensor([e2e_ms], device=dev)
+    dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t_max.item())
+    # NCCL on the same message, for the algorithm table (not the product path)
+    nccl_bus = None
+    if op in ("all_reduce", "all_gather", "reduce_scatter"):
+        a = torch.empty(in_numel, dtype=dtype, device=dev).copy_(x)
+        o = torch.empty(out_numel, dtype=dtype, device=dev)
+
+        def nstep():
+            if op == "all_reduce":
+                dist.all_reduce(a)
+            elif op == "reduce_scatter":
+                dist.reduce_scatter_tensor(o, a)
+            else:
+                dist.all_gather_into_tensor(o, a) if len(set(lens)) == 1 else None
+
+        for _ in range(3):
+            nstep()
+        torch.cuda.synchronize()
+        dist.barrier()
+        nms = time_steps(nstep, max(5, args.steps // 2), stream)
+        t_max = torch.tensor([nms], device=dev)
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        nccl_bus = msg * bus_factor(op, n) / (float(t_max.item()) / 1e3) / 1e9
+    bus = msg * bus_factor(op, n) / (ms / 1e3) / 1e9
+    e2e_bus = msg * bus_factor(op, n) / (e2e_ms / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "redistribute bus GB/s",
+            "value": round(bus * n, 2),
+            "unit": "GB/s",
+            "n_gpus": n,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": DT_NAME[dtype],
+            "data": "synthetic (seeded, BASELINE.json distribution)",
+            "config": {"workload": cfg["name"] + f" on {n} GPUs, one rank per GPU, P2P kernels over NVLink",
+                       "op": op, "group_ranks": n, "msg_bytes_per_rank": msg,
+                       "l2": "per-rank buffers larger than L2; no flush", "parallelism": f"group{n}"},
+            "bus_gbs_per_rank": round(bus, 2),
+            "pct_nvlink_peak": round(bus / NVLINK_NOMINAL_GBS, 4),
+            "nccl_bus_gbs_per_rank": None if nccl_bus is None else round(nccl_bus, 2),
+            "roofline": {"bound": "nvlink", "achieved": round(bus, 1), "peak": NVLINK_PEER_COPY_GBS, "unit": "GB/s",
+                         "frac": round(bus / NVLINK_PEER_COPY_GBS, 4), "traffic": None,
+                         "peak_source": "measured peer copy per direction (pool reference); nominal 900"},
+            "e2e": {"value": round(e2e_bus * n, 3), "unit": "GB/s", "h2d_bytes_per_step": in_numel * es,
+                    "d2h_bytes_per_step": out_numel * es, "ms_per_step": round(e2e_ms, 4),
+                    "path": "C ABI (dt_* on a multi-process dt_comm) with pinned host buffers"},
+            "gpu_launches": launches,
+            "device_error": err,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    comm.destroy()
+    dist.destroy_process_group()
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--op", choices=list(CONFIGS), default="all_reduce")
+    p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
+    p.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end leg (profiling runs)")
+    args = p.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        run_ours_multi(args, rank, world, local_rank)
+    else:
+        run_ours_single(args)
+
+
+if __name__ == "__main__":
+    main()

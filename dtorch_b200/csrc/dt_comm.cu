@@ -1,0 +1,1219 @@
+// Host side of the C ABI declared in include/dtorch_b200.h: communicators, peer mapping, per-call pointer
+// rendezvous, kernel selection and launch.
+//
+// Reference interfaces replaced (tingkuanpei/dtorch):
+//   ThreadGroup ctor / backend choice        dtorch/core/communication/thread_group/thread_group.cc:61-90
+//   ThreadGroup::AllReduce                   thread_group.cc:127-141
+//   ThreadGroup::EqualShapeAllGatherIntoTensor / AllGather / AllGatherIntoVec   thread_group.cc:151-190
+//   ThreadGroup::ReduceScatterTensor         thread_group.cc:192-209
+//   ThreadGroup::AllToAll                    thread_group.cc:211-241
+//   ThreadGroup::Barrier                     thread_group.cc:118-125
+//   ThreadGroupSameDeviceBackend             thread_group_same_device_backend.cc:71-360
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/dtorch_b200.h"
+#include "dt_kernels.cuh"
+
+using namespace dtb;
+
+namespace {
+
+thread_local std::string g_err;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int status, const std::string& msg) {
+    g_err = msg;
+    return status;
+}
+
+#define DT_CUDA(call)                                                                          \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess) {                                                               \
+            return fail(DT_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));      \
+        }                                                                                      \
+    } while (0)
+
+constexpr size_t kFlagBytes = static_cast<size_t>(kMaxBlocks) * kMaxRanks * sizeof(uint32_t);
+constexpr size_t kHeapOffset = 64 * 1024;  // heap starts 64 KiB into the slab (flags first)
+constexpr uint32_t kHandleMagic = 0x44544232u;  // "DTB2"
+
+int elem_bytes(int dtype) {
+    switch (dtype) {
+        case DT_FLOAT32: return 4;
+        case DT_BFLOAT16: return 2;
+        case DT_FLOAT16: return 2;
+        default: return 0;
+    }
+}
+
+struct IpcHandle {
+    uint32_t magic;
+    int32_t rank;
+    int32_t nranks;
+    int32_t pad;
+    uint64_t heap_bytes;
+    cudaIpcMemHandle_t mem;
+};
+
+// Per-rank state. In a single-process communicator every rank's entry is filled; in a multi-process one only
+// the local rank's entry owns memory and peer pointers come from IPC mappings.
+struct RankState {
+    int dev = -1;
+    int num_sms = 148;
+    char* slab = nullptr;         // cudaMalloc'd: [flags | pad | heap]
+    uint32_t* flags = nullptr;    // this rank's flag array (on dev)
+    char* heap = nullptr;
+    int* err = nullptr;           // host-mapped error word
+    uint32_t epoch = 0;           // collectives issued by this rank
+    uint64_t rv_gen = 0;          // rendezvous generations passed by this rank
+    cudaEvent_t ready = nullptr;  // same-device mode
+    uint32_t* peer_flags[kMaxRanks] = {};  // flags of rank r as addressed from this rank's device
+    char* peer_heap[kMaxRanks] = {};       // heap of rank r as addressed from this rank's device
+    bool imported[kMaxRanks] = {};         // peer slab opened through IPC (must be closed)
+};
+
+// What one rank publishes at a rendezvous.
+struct Slot {
+    const void* in;
+    void* out;
+    cudaStream_t stream;
+};
+
+}  // namespace
+
+struct dt_comm {
+    int n = 0;
+    bool same_device = false;
+    bool multiprocess = false;
+    bool ready = false;
+    std::atomic<bool> broken{false};
+    int local_rank = -1;  // multi-process: the rank this process holds
+    size_t heap_bytes = 0;
+    int64_t timeout_ms = 600000;
+    RankState r[kMaxRanks];
+    // in-process rendezvous: double-buffered slots indexed by generation parity
+    Slot slots[2][kMaxRanks];
+    std::atomic<int> arrived[2];
+    std::atomic<uint64_t> gen{0};
+    // same-device mode: rank 0 launches, others wait for this generation and chain on `done`
+    cudaEvent_t done = nullptr;
+    std::atomic<uint64_t> launched_gen{0};
+    std::atomic<int> launch_status{0};
+};
+
+namespace {
+
+int64_t env_timeout_ms() {
+    const char* s = std::getenv("DTORCH_COMM_TIMEOUT_SECOND");
+    if (s != nullptr && *s != '\0') {
+        long long v = std::atoll(s);
+        if (v > 0) return static_cast<int64_t>(v) * 1000;
+    }
+    return 600 * 1000;  // the reference's default (global_option.cc:20)
+}
+
+bool check_rank(const dt_comm* c, int rank) {
+    if (c == nullptr || rank < 0 || rank >= c->n) return false;
+    if (c->multiprocess && rank != c->local_rank) return false;
+    return true;
+}
+
+int alloc_rank(dt_comm* c, int rank, int dev, size_t heap_bytes) {
+    RankState& s = c->r[rank];
+    s.dev = dev;
+    DT_CUDA(cudaSetDevice(dev));
+    DT_CUDA(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    const size_t bytes = kHeapOffset + heap_bytes;
+    DT_CUDA(cudaMalloc(&s.slab, bytes));
+    DT_CUDA(cudaMemset(s.slab, 0, kFlagBytes));
+    s.flags = reinterpret_cast<uint32_t*>(s.slab);
+    s.heap = s.slab + kHeapOffset;
+    DT_CUDA(cudaHostAlloc(&s.err, sizeof(int) * 4, cudaHostAllocMapped | cudaHostAllocPortable));
+    *reinterpret_cast<volatile int*>(s.err) = 0;
+    DT_CUDA(cudaEventCreateWithFlags(&s.ready, cudaEventDisableTiming));
+    DT_CUDA(cudaDeviceSynchronize());
+    return DT_OK;
+}
+
+// Largest grid whose blocks are all resident at once (every block of a barrier kernel waits for the block
+// with the same index on every peer, so all of them must be running).
+template <typename K>
+int resident_grid(K kernel, int dev, int num_sms) {
+    static std::mutex m;
+    static std::unordered_map<uint64_t, int> cache;
+    const uint64_t key = (reinterpret_cast<uint64_t>(reinterpret_cast<const void*>(kernel)) << 4) ^ static_cast<uint64_t>(dev);
+    {
+        std::lock_guard<std::mutex> g(m);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    const int g = std::min(per_sm * num_sms, kMaxBlocks);
+    std::lock_guard<std::mutex> lk(m);
+    cache[key] = g;
+    return g;
+}
+
+SignalCtx make_sig(dt_comm* c, int rank) {
+    SignalCtx s{};
+    for (int i = 0; i < kMaxRanks; ++i) s.flags[i] = c->r[rank].peer_flags[i];
+    s.err = c->r[rank].err;
+    s.rank = rank;
+    s.n = c->n;
+    s.timeout_ns = static_cast<uint64_t>(c->timeout_ms) * 1000000ull;
+    return s;
+}
+
+// In-process rendezvous of all ranks of a single-process communicator: every rank publishes its Slot and
+// receives everyone's. Spins (yielding) with the communicator timeout; a timeout marks the communicator
+// broken because the generation count can no longer agree across ranks.
+int rendezvous(dt_comm* c, int rank, const Slot& mine, Slot* all) {
+    RankState& s = c->r[rank];
+    const uint64_t my_gen = s.rv_gen;
+    const int buf = static_cast<int>(my_gen & 1);
+    c->slots[buf][rank] = mine;
+    if (c->arrived[buf].fetch_add(1, std::memory_order_acq_rel) + 1 == c->n) {
+        c->arrived[buf].store(0, std::memory_order_relaxed);
+        c->gen.store(my_gen + 1, std::memory_order_release);
+    } else {
+        const auto t0 = std::chrono::steady_clock::now();
+        uint32_t spins = 0;
+        while (c->gen.load(std::memory_order_acquire) <= my_gen) {
+            if (++spins > 256) {
+                std::this_thread::yield();
+                if ((spins & 1023) == 0) {
+                    const auto dt = std::chrono::steady_clock::now() - t0;
+                    if (std::chrono::duration_cast<std::chrono::milliseconds>(dt).count() > c->timeout_ms) {
+                        c->broken = true;
+                        return fail(DT_ERR_TIMEOUT, "rendezvous: a rank did not arrive within the timeout");
+                    }
+                }
+            }
+        }
+    }
+    for (int i = 0; i < c->n; ++i) all[i] = c->slots[buf][i];
+    s.rv_gen = my_gen + 1;
+    return DT_OK;
+}
+
+bool in_heap(const dt_comm* c, int rank, const void* p, size_t bytes) {
+    const RankState& s = c->r[rank];
+    if (s.heap == nullptr || c->heap_bytes == 0) return false;
+    const char* q = static_cast<const char*>(p);
+    return q >= s.heap && q + bytes <= s.heap + c->heap_bytes;
+}
+
+// Resolve every rank's in/out pointer as addressed from `rank`'s device: symmetric-heap offsets when both
+// buffers live in the heap, otherwise (single process only) the per-call rendezvous.
+int resolve_peers(dt_comm* c, int rank, const void* in, size_t in_bytes, void* out, size_t out_bytes,
+                  const char** ins, char** outs) {
+    RankState& s = c->r[rank];
+    const bool heap_in = in_bytes == 0 || in_heap(c, rank, in, in_bytes);
+    const bool heap_out = out_bytes == 0 || in_heap(c, rank, out, out_bytes);
+    if (heap_in && heap_out) {
+        const ptrdiff_t oi = static_cast<const char*>(in) - s.heap;
+        const ptrdiff_t oo = static_cast<char*>(out) - s.heap;
+        for (int r = 0; r < c->n; ++r) {
+            ins[r] = s.peer_heap[r] + oi;
+            outs[r] = s.peer_heap[r] + oo;
+        }
+        return DT_OK;
+    }
+    if (c->multiprocess) {
+        return fail(DT_ERR_INVALID, "multi-process communicator: buffers must live in the symmetric heap");
+    }
+    Slot all[kMaxRanks];
+    int st = rendezvous(c, rank, Slot{in, out, nullptr}, all);
+    if (st != DT_OK) return st;
+    for (int r = 0; r < c->n; ++r) {
+        ins[r] = static_cast<const char*>(all[r].in);
+        outs[r] = static_cast<char*>(all[r].out);
+    }
+    return DT_OK;
+}
+
+int launch_check(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(DT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return DT_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Reduction launches
+// ---------------------------------------------------------------------------------------------------------
+// Grid of a launch. Barrier kernels pair block b of every rank with block b of every peer, so (1) every rank
+// must launch the same grid -- callers pass `want_blocks` computed from sizes every rank knows -- and (2) all
+// blocks must be resident at once, which the per-SM cap guarantees (checked against the occupancy of the
+// variant; variants are chosen from rank-independent parameters).
+template <typename K>
+int pick_grid(K kernel, int dev, int num_sms, int64_t want_blocks, int per_sm_cap, int* grid) {
+    const int occ = resident_grid(kernel, dev, num_sms) / std::max(num_sms, 1);
+    const int per_sm = std::min(per_sm_cap, std::max(occ, 1));
+    const int64_t cap = std::min<int64_t>(static_cast<int64_t>(per_sm) * num_sms, kMaxBlocks);
+    *grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want_blocks, cap)));
+    return DT_OK;
+}
+
+constexpr int kReduceBlocksPerSM = 2;
+constexpr int kCopyBlocksPerSM = 2;
+
+template <int NR>
+constexpr int reduce_unroll() { return NR <= 2 ? 4 : 2; }
+
+int64_t reduce_want_blocks(int64_t vectors, int64_t scalars, int nr) {
+    const int64_t u = nr <= 2 ? 4 : 2;
+    const int64_t vb = (vectors + kThreads * u - 1) / (kThreads * u);
+    const int64_t sb = (scalars + kThreads - 1) / kThreads;
+    return std::max<int64_t>(1, std::max(vb, sb));
+}
+
+template <int DT, int NR, bool ST, bool BAR>
+int launch_reduce_t(const ReduceArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks) {
+    auto k = k_reduce<DT, NR, ST, BAR>;
+    if (want_blocks <= 0) want_blocks = reduce_want_blocks(a.vhi - a.vlo, a.shi - a.slo, NR);
+    int grid = 1;
+    pick_grid(k, dev, num_sms, want_blocks, kReduceBlocksPerSM, &grid);
+    k<<<grid, kThreads, 0, stream>>>(a);
+    return launch_check("k_reduce");
+}
+
+template <int DT, bool ST, bool BAR>
+int launch_reduce_nr(const ReduceArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want) {
+    if (a.n <= 2) return launch_reduce_t<DT, 2, ST, BAR>(a, dev, num_sms, stream, want);
+    if (a.n <= 4) return launch_reduce_t<DT, 4, ST, BAR>(a, dev, num_sms, stream, want);
+    return launch_reduce_t<DT, 8, ST, BAR>(a, dev, num_sms, stream, want);
+}
+
+// want_blocks <= 0: size the grid from this launch's own ranges (same-device kernels, no barrier).
+template <bool BAR>
+int launch_reduce(const ReduceArgs& a, int dtype, bool storage, int dev, int num_sms, cudaStream_t stream,
+                  int64_t want_blocks = 0) {
+    switch (dtype) {
+        case DT_FLOAT32:
+            return launch_reduce_nr<0, false, BAR>(a, dev, num_sms, stream, want_blocks);
+        case DT_BFLOAT16:
+            return storage ? launch_reduce_nr<1, true, BAR>(a, dev, num_sms, stream, want_blocks)
+                           : launch_reduce_nr<1, false, BAR>(a, dev, num_sms, stream, want_blocks);
+        case DT_FLOAT16:
+            return storage ? launch_reduce_nr<2, true, BAR>(a, dev, num_sms, stream, want_blocks)
+                           : launch_reduce_nr<2, false, BAR>(a, dev, num_sms, stream, want_blocks);
+        default:
+            return fail(DT_ERR_INVALID, "unsupported dtype");
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Fill the vector / scalar ranges for reducing elements [lo, hi) of the inputs. Vectors are used when every
+// input and output base is 16-byte aligned and the range starts on a vector boundary; the remainder is scalar.
+void set_ranges(ReduceArgs& a, int64_t lo, int64_t hi, int per_vec, bool vec_ok) {
+    if (!vec_ok || lo % per_vec != 0) {
+        a.vlo = a.vhi = 0;
+        a.slo = lo;
+        a.shi = hi;
+        return;
+    }
+    a.vlo = lo / per_vec;
+    a.vhi = hi / per_vec;
+    a.slo = a.vhi * per_vec;
+    a.shi = hi;
+    if (a.vhi < a.vlo) a.vhi = a.vlo;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Copy launches
+// ---------------------------------------------------------------------------------------------------------
+uint64_t gcd_u64(uint64_t a, uint64_t b) {
+    while (b != 0) {
+        const uint64_t t = a % b;
+        a = b;
+        b = t;
+    }
+    return a;
+}
+
+void finish_seg(Seg& s, int vw_unused) {
+    (void)vw_unused;
+    // Merge adjacent row dims that are contiguous on both sides, then fold contiguous rows into the run.
+    for (int pass = 0; pass < 2; ++pass) {
+        for (int d = 1; d >= 0; --d) {
+            if (s.cnt[d] > 1 && s.cnt[d + 1] > 1 && s.ss[d] == s.cnt[d + 1] * s.ss[d + 1] &&
+                s.ds[d] == s.cnt[d + 1] * s.ds[d + 1]) {
+                s.cnt[d + 1] *= s.cnt[d];
+                s.cnt[d] = 1;
+                s.ss[d] = s.ds[d] = 0;
+            }
+        }
+        // move a lone row dim to slot 2 (fast path in the kernel)
+        if (s.cnt[2] == 1) {
+            for (int d = 1; d >= 0; --d) {
+                if (s.cnt[d] > 1) {
+                    std::swap(s.cnt[d], s.cnt[2]);
+                    std::swap(s.ss[d], s.ss[2]);
+                    std::swap(s.ds[d], s.ds[2]);
+                    break;
+                }
+            }
+        }
+    }
+    if (s.cnt[0] == 1 && s.cnt[1] == 1 && s.cnt[2] > 1 && s.ss[2] == s.run && s.ds[2] == s.run) {
+        s.run *= s.cnt[2];
+        s.cnt[2] = 1;
+        s.ss[2] = s.ds[2] = 0;
+    }
+}
+
+uint64_t seg_align(const Seg& s) {
+    uint64_t g = reinterpret_cast<uint64_t>(s.src) | reinterpret_cast<uint64_t>(s.dst);
+    g = gcd_u64(g == 0 ? 16 : g, static_cast<uint64_t>(s.run));
+    for (int d = 0; d < 3; ++d) {
+        if (s.cnt[d] > 1) {
+            g = gcd_u64(g, static_cast<uint64_t>(s.ss[d]));
+            g = gcd_u64(g, static_cast<uint64_t>(s.ds[d]));
+        }
+    }
+    return g;
+}
+
+// Items of a segment set counted with 2 KiB items (the 16-byte geometry) -- the rank-independent size
+// measure barrier launches use for their grid.
+int64_t copy_want_blocks(int64_t max_row_bytes, int64_t rows, int nseg) {
+    constexpr int64_t seg = CopyGeom<16>::kSegBytes;
+    const int64_t items = rows * ((max_row_bytes + seg - 1) / seg);
+    const int64_t warps = kThreads / 32;
+    return std::max<int64_t>(1, (items * nseg + warps - 1) / warps);
+}
+
+template <int VW, int MAXSEG, bool BAR>
+int launch_copy_t(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks) {
+    constexpr int SEGB = CopyGeom<VW>::kSegBytes;
+    a.max_items = 0;
+    for (int i = 0; i < a.nseg; ++i) {
+        Seg& s = a.seg[i];
+        const int64_t rows = s.cnt[0] * s.cnt[1] * s.cnt[2];
+        s.spr = s.run > 0 ? (s.run + SEGB - 1) / SEGB : 0;
+        s.items = rows * s.spr;
+        a.max_items = std::max(a.max_items, s.items);
+    }
+    auto k = k_copy<VW, MAXSEG, BAR>;
+    if (want_blocks <= 0) {
+        const int64_t warps_per_block = kThreads / 32;
+        want_blocks = std::max<int64_t>((a.max_items * a.nseg + warps_per_block - 1) / warps_per_block, 1);
+    }
+    int grid = 1;
+    pick_grid(k, dev, num_sms, want_blocks, kCopyBlocksPerSM, &grid);
+    k<<<grid, kThreads, 0, stream>>>(a);
+    return launch_check("k_copy");
+}
+
+template <int MAXSEG, bool BAR>
+int launch_copy(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks = 0) {
+    uint64_t g = 16;
+    for (int i = 0; i < a.nseg; ++i) {
+        finish_seg(a.seg[i], 0);
+        if (a.seg[i].run > 0) g = gcd_u64(g, seg_align(a.seg[i]));
+    }
+    if (g % 16 == 0) return launch_copy_t<16, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
+    if (g % 8 == 0) return launch_copy_t<8, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
+    if (g % 4 == 0) return launch_copy_t<4, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
+    if (g % 2 == 0) return launch_copy_t<2, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
+    return launch_copy_t<1, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
+}
+
+// Shard sizes: the first L % n ranks get one more (Placement::GetShardSizeForAllRank,
+// dtorch/api/cpp/distributed_spec.cc:202-213).
+void shard_sizes(int64_t L, int n, int64_t* out) {
+    for (int i = 0; i < n; ++i) out[i] = L / n + (i < L % n ? 1 : 0);
+}
+
+// All-to-all segment from source rank i (input base `src`) to destination rank k (output base `dst`).
+// The tensor is viewed as [d0, X, dmid, Y, d2] with X/Y the src/dst dims in their order in the shape.
+struct A2AGeom {
+    int64_t d0, dmid, d2;
+    int64_t D;      // dst-dim extent (same on every rank of the group)
+    int64_t A;      // src-dim extent of the output (sum of src_lens)
+    bool src_first; // src_dim < dst_dim
+    int64_t es;
+};
+
+Seg a2a_seg(const A2AGeom& g, const char* src, char* dst, int64_t L_i, int64_t soff_i, int64_t len_k, int64_t off_k) {
+    Seg s{};
+    s.src = src;
+    s.dst = dst;
+    const int64_t es = g.es;
+    if (g.src_first) {
+        // in: [d0, L_i, dmid, D, d2]  -> rows (p, x, q), run = len_k*d2
+        // out: [d0, A, dmid, len_k, d2]
+        s.run = len_k * g.d2 * es;
+        s.cnt[0] = g.d0;
+        s.cnt[1] = L_i;
+        s.cnt[2] = g.dmid;
+        s.ss[2] = g.D * g.d2 * es;
+        s.ss[1] = g.dmid * s.ss[2];
+        s.ss[0] = L_i * s.ss[1];
+        s.ds[2] = len_k * g.d2 * es;
+        s.ds[1] = g.dmid * s.ds[2];
+        s.ds[0] = g.A * s.ds[1];
+        s.src += off_k * g.d2 * es;
+        s.dst += soff_i * s.ds[1];
+    } else {
+        // in: [d0, D, dmid, L_i, d2]  -> rows (p, y, q), run = L_i*d2
+        // out: [d0, len_k, dmid, A, d2]
+        s.run = L_i * g.d2 * es;
+        s.cnt[0] = g.d0;
+        s.cnt[1] = len_k;
+        s.cnt[2] = g.dmid;
+        s.ss[2] = L_i * g.d2 * es;
+        s.ss[1] = g.dmid * s.ss[2];
+        s.ss[0] = g.D * s.ss[1];
+        s.ds[2] = g.A * g.d2 * es;
+        s.ds[1] = g.dmid * s.ds[2];
+        s.ds[0] = len_k * s.ds[1];
+        s.src += off_k * s.ss[1];
+        s.dst += soff_i * g.d2 * es;
+    }
+    if (s.run == 0 || s.cnt[0] == 0 || s.cnt[1] == 0 || s.cnt[2] == 0) {
+        s.run = 0;
+        s.cnt[0] = s.cnt[1] = s.cnt[2] = 1;
+    }
+    return s;
+}
+
+int a2a_geom(int n, int ndim, const int64_t* in_shape, int src_dim, int dst_dim, const int64_t* src_lens,
+             size_t elem_b, A2AGeom* g) {
+    if (ndim < 2 || ndim > 16 || in_shape == nullptr || src_lens == nullptr) return fail(DT_ERR_INVALID, "a2a: bad shape");
+    if (src_dim < 0 || src_dim >= ndim || dst_dim < 0 || dst_dim >= ndim || src_dim == dst_dim)
+        return fail(DT_ERR_INVALID, "a2a: src_dim/dst_dim out of range or equal");
+    if (elem_b == 0) return fail(DT_ERR_INVALID, "a2a: elem_bytes == 0");
+    for (int d = 0; d < ndim; ++d)
+        if (in_shape[d] < 0) return fail(DT_ERR_INVALID, "a2a: negative extent");
+    const int lo = std::min(src_dim, dst_dim), hi = std::max(src_dim, dst_dim);
+    g->d0 = 1;
+    g->dmid = 1;
+    g->d2 = 1;
+    for (int d = 0; d < lo; ++d) g->d0 *= in_shape[d];
+    for (int d = lo + 1; d < hi; ++d) g->dmid *= in_shape[d];
+    for (int d = hi + 1; d < ndim; ++d) g->d2 *= in_shape[d];
+    g->D = in_shape[dst_dim];
+    g->A = 0;
+    for (int r = 0; r < n; ++r) {
+        if (src_lens[r] < 0) return fail(DT_ERR_INVALID, "a2a: negative src_lens");
+        g->A += src_lens[r];
+    }
+    g->src_first = src_dim < dst_dim;
+    g->es = static_cast<int64_t>(elem_b);
+    if (g->D < n) return fail(DT_ERR_INVALID, "a2a: dst dim smaller than the group (reference asserts size >= n)");
+    return DT_OK;
+}
+
+// Same-device mode: rank 0 launches one kernel for the whole group after every rank's stream reached the
+// call (its `ready` event); the others chain their streams on `done`. `body` issues the kernel on rank 0's
+// stream given every rank's Slot.
+template <typename Body>
+int same_device_call(dt_comm* c, int rank, const void* in, void* out, cudaStream_t stream, Body body) {
+    RankState& s = c->r[rank];
+    DT_CUDA(cudaSetDevice(s.dev));
+    DT_CUDA(cudaEventRecord(s.ready, stream));
+    const uint64_t my_gen = s.rv_gen;
+    Slot all[kMaxRanks];
+    int st = rendezvous(c, rank, Slot{in, out, stream}, all);
+    if (st != DT_OK) return st;
+    if (rank == 0) {
+        int rc = DT_OK;
+        for (int r = 1; r < c->n && rc == DT_OK; ++r)
+            if (cudaStreamWaitEvent(stream, c->r[r].ready, 0) != cudaSuccess) rc = fail(DT_ERR_CUDA, "cudaStreamWaitEvent");
+        if (rc == DT_OK) rc = body(all, stream);
+        if (rc == DT_OK && cudaEventRecord(c->done, stream) != cudaSuccess) rc = fail(DT_ERR_CUDA, "cudaEventRecord");
+        c->launch_status.store(rc, std::memory_order_relaxed);
+        c->launched_gen.store(my_gen + 1, std::memory_order_release);
+        return rc;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    uint32_t spins = 0;
+    while (c->launched_gen.load(std::memory_order_acquire) <= my_gen) {
+        if (++spins > 256) {
+            std::this_thread::yield();
+            if ((spins & 1023) == 0 &&
+                std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count() >
+                    c->timeout_ms) {
+                c->broken = true;
+                return fail(DT_ERR_TIMEOUT, "same-device: launch by rank 0 not seen within the timeout");
+            }
+        }
+    }
+    const int rc = c->launch_status.load(std::memory_order_relaxed);
+    if (rc != DT_OK) return fail(rc, "same-device: rank 0 failed to launch the collective");
+    DT_CUDA(cudaStreamWaitEvent(stream, c->done, 0));
+    return DT_OK;
+}
+
+int common_checks(dt_comm* c, int rank) {
+    if (c == nullptr) return fail(DT_ERR_INVALID, "null communicator");
+    if (!check_rank(c, rank)) return fail(DT_ERR_INVALID, "rank out of range for this communicator");
+    if (c->broken) return fail(DT_ERR_STATE, "communicator is broken by an earlier timeout");
+    if (!c->ready) return fail(DT_ERR_STATE, "communicator not ready (import peers first)");
+    return DT_OK;
+}
+
+// Local (single-device) reduce with `nout` outputs, elements [0, count).
+int local_reduce(int n, const char* const* ins, char* const* outs, int nout, size_t count, int dtype, int flags,
+                 cudaStream_t stream, int dev, int num_sms) {
+    ReduceArgs a{};
+    const int pv = 16 / elem_bytes(dtype);
+    bool vec_ok = true;
+    for (int r = 0; r < n; ++r) {
+        a.in[r] = ins[r];
+        vec_ok = vec_ok && aligned16(ins[r]);
+    }
+    for (int j = 0; j < nout; ++j) {
+        a.out[j] = outs[j];
+        vec_ok = vec_ok && aligned16(outs[j]);
+    }
+    a.n = n;
+    a.nout = nout;
+    a.out_shift = 0;
+    set_ranges(a, 0, static_cast<int64_t>(count), pv, vec_ok);
+    return launch_reduce<false>(a, dtype, (flags & DT_ACCUM_STORAGE) != 0, dev, num_sms, stream);
+}
+
+int current_device_sms(int* dev, int* sms) {
+    DT_CUDA(cudaGetDevice(dev));
+    DT_CUDA(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, *dev));
+    return DT_OK;
+}
+
+}  // namespace
+
+// =============================================================================================================
+// C ABI
+// =============================================================================================================
+extern "C" {
+
+const char* dt_status_string(int status) {
+    switch (status) {
+        case DT_OK: return "ok";
+        case DT_ERR_INVALID: return "invalid argument";
+        case DT_ERR_CUDA: return "CUDA error";
+        case DT_ERR_TIMEOUT: return "timeout waiting for a peer";
+        case DT_ERR_PEER: return "peer access unavailable";
+        case DT_ERR_UNSUPPORTED: return "unsupported";
+        case DT_ERR_STATE: return "communicator not usable";
+        default: return "unknown status";
+    }
+}
+
+const char* dt_last_error_message(void) { return g_err.c_str(); }
+
+int dt_version(void) { return (1 << 16) | 0; }
+
+uint64_t dt_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_comm** out) {
+    if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
+    *out = nullptr;
+    if (nranks < 1 || nranks > kMaxRanks || cuda_devices == nullptr) return fail(DT_ERR_INVALID, "nranks must be 1..8");
+    int ndev = 0;
+    DT_CUDA(cudaGetDeviceCount(&ndev));
+    bool same = true;
+    for (int i = 0; i < nranks; ++i) {
+        if (cuda_devices[i] < 0 || cuda_devices[i] >= ndev) return fail(DT_ERR_INVALID, "device id out of range");
+        if (cuda_devices[i] != cuda_devices[0]) same = false;
+        for (int j = 0; j < i; ++j)
+            if (!same && cuda_devices[j] == cuda_devices[i])
+                return fail(DT_ERR_INVALID, "devices must be all equal (same-device mode) or all distinct");
+    }
+    if (!same) {
+        for (int i = 0; i < nranks; ++i)
+            for (int j = 0; j < i; ++j)
+                if (cuda_devices[j] == cuda_devices[i])
+                    return fail(DT_ERR_INVALID, "devices must be all equal (same-device mode) or all distinct");
+    }
+    dt_comm* c = new dt_comm();
+    c->n = nranks;
+    c->same_device = same && nranks > 1;
+    c->heap_bytes = heap_bytes;
+    c->timeout_ms = env_timeout_ms();
+    c->arrived[0] = 0;
+    c->arrived[1] = 0;
+    int st = DT_OK;
+    for (int i = 0; i < nranks && st == DT_OK; ++i) st = alloc_rank(c, i, cuda_devices[i], c->same_device ? 0 : heap_bytes);
+    if (st == DT_OK && c->same_device) {
+        cudaSetDevice(cuda_devices[0]);
+        if (cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming) != cudaSuccess) st = fail(DT_ERR_CUDA, "event");
+    }
+    if (st == DT_OK && !c->same_device) {
+        for (int i = 0; i < nranks && st == DT_OK; ++i) {
+            cudaSetDevice(cuda_devices[i]);
+            for (int j = 0; j < nranks; ++j) {
+                if (i == j) continue;
+                int can = 0;
+                cudaDeviceCanAccessPeer(&can, cuda_devices[i], cuda_devices[j]);
+                if (!can) {
+                    st = fail(DT_ERR_PEER, "cudaDeviceCanAccessPeer = 0");
+                    break;
+                }
+                cudaError_t e = cudaDeviceEnablePeerAccess(cuda_devices[j], 0);
+                if (e == cudaErrorPeerAccessAlreadyEnabled) {
+                    cudaGetLastError();
+                } else if (e != cudaSuccess) {
+                    st = fail(DT_ERR_PEER, std::string("cudaDeviceEnablePeerAccess: ") + cudaGetErrorString(e));
+                    break;
+                }
+            }
+        }
+        for (int i = 0; i < nranks; ++i)
+            for (int j = 0; j < nranks; ++j) {
+                c->r[i].peer_flags[j] = c->r[j].flags;
+                c->r[i].peer_heap[j] = c->r[j].heap;
+            }
+    }
+    if (st != DT_OK) {
+        std::string msg = g_err;
+        dt_comm_destroy(c);
+        g_err = msg;
+        return st;
+    }
+    c->ready = true;
+    *out = c;
+    return DT_OK;
+}
+
+int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes, dt_comm** out) {
+    if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
+    *out = nullptr;
+    if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks) return fail(DT_ERR_INVALID, "bad rank/nranks");
+    dt_comm* c = new dt_comm();
+    c->n = nranks;
+    c->multiprocess = true;
+    c->local_rank = rank;
+    c->heap_bytes = heap_bytes;
+    c->timeout_ms = env_timeout_ms();
+    int st = alloc_rank(c, rank, cuda_device, heap_bytes);
+    if (st != DT_OK) {
+        std::string msg = g_err;
+        dt_comm_destroy(c);
+        g_err = msg;
+        return st;
+    }
+    c->r[rank].peer_flags[rank] = c->r[rank].flags;
+    c->r[rank].peer_heap[rank] = c->r[rank].heap;
+    c->ready = nranks == 1;
+    *out = c;
+    return DT_OK;
+}
+
+size_t dt_comm_handle_bytes(void) { return sizeof(IpcHandle); }
+
+int dt_comm_export(dt_comm* c, void* handle) {
+    if (c == nullptr || handle == nullptr || !c->multiprocess) return fail(DT_ERR_INVALID, "export needs a multi-process communicator");
+    RankState& s = c->r[c->local_rank];
+    IpcHandle h{};
+    h.magic = kHandleMagic;
+    h.rank = c->local_rank;
+    h.nranks = c->n;
+    h.heap_bytes = c->heap_bytes;
+    DT_CUDA(cudaSetDevice(s.dev));
+    DT_CUDA(cudaIpcGetMemHandle(&h.mem, s.slab));
+    std::memcpy(handle, &h, sizeof(h));
+    return DT_OK;
+}
+
+int dt_comm_import(dt_comm* c, const void* handles) {
+    if (c == nullptr || handles == nullptr || !c->multiprocess) return fail(DT_ERR_INVALID, "import needs a multi-process communicator");
+    const int me = c->local_rank;
+    RankState& s = c->r[me];
+    DT_CUDA(cudaSetDevice(s.dev));
+    const IpcHandle* hs = static_cast<const IpcHandle*>(handles);
+    for (int r = 0; r < c->n; ++r) {
+        if (r == me) continue;
+        const IpcHandle& h = hs[r];
+        if (h.magic != kHandleMagic || h.rank != r || h.nranks != c->n || h.heap_bytes != c->heap_bytes)
+            return fail(DT_ERR_INVALID, "import: handle does not match this communicator");
+        if (s.imported[r]) continue;
+        void* p = nullptr;
+        DT_CUDA(cudaIpcOpenMemHandle(&p, h.mem, cudaIpcMemLazyEnablePeerAccess));
+        s.imported[r] = true;
+        s.peer_flags[r] = reinterpret_cast<uint32_t*>(p);
+        s.peer_heap[r] = static_cast<char*>(p) + kHeapOffset;
+    }
+    c->ready = true;
+    return DT_OK;
+}
+
+int dt_comm_destroy(dt_comm* c) {
+    if (c == nullptr) return DT_OK;
+    for (int i = 0; i < kMaxRanks; ++i) {
+        RankState& s = c->r[i];
+        if (s.dev < 0) continue;
+        cudaSetDevice(s.dev);
+        cudaDeviceSynchronize();
+        for (int j = 0; j < kMaxRanks; ++j)
+            if (s.imported[j]) cudaIpcCloseMemHandle(s.peer_flags[j]);
+        if (s.ready) cudaEventDestroy(s.ready);
+        if (s.slab) cudaFree(s.slab);
+        if (s.err) cudaFreeHost(s.err);
+    }
+    if (c->done) cudaEventDestroy(c->done);
+    cudaGetLastError();
+    delete c;
+    return DT_OK;
+}
+
+int dt_comm_size(const dt_comm* c) { return c ? c->n : 0; }
+
+int dt_comm_same_device(const dt_comm* c) { return (c && c->same_device) ? 1 : 0; }
+
+int dt_comm_heap(dt_comm* c, int rank, void** base, size_t* bytes) {
+    if (c == nullptr || !check_rank(c, rank) || base == nullptr || bytes == nullptr) return fail(DT_ERR_INVALID, "bad args");
+    *base = c->r[rank].heap;
+    *bytes = c->same_device ? 0 : c->heap_bytes;
+    return DT_OK;
+}
+
+int dt_comm_set_timeout_ms(dt_comm* c, int64_t ms) {
+    if (c == nullptr || ms <= 0) return fail(DT_ERR_INVALID, "timeout must be > 0");
+    c->timeout_ms = ms;
+    return DT_OK;
+}
+
+int dt_comm_error(dt_comm* c, int rank) {
+    if (c == nullptr || !check_rank(c, rank)) return DT_ERR_INVALID;
+    return *reinterpret_cast<volatile int*>(c->r[rank].err);
+}
+
+int dt_comm_clear_error(dt_comm* c, int rank) {
+    if (c == nullptr || !check_rank(c, rank)) return fail(DT_ERR_INVALID, "bad rank");
+    *reinterpret_cast<volatile int*>(c->r[rank].err) = 0;
+    return DT_OK;
+}
+
+// ---- all-reduce / reduce-scatter ---------------------------------------------------------------------------
+
+int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count, int dtype, int op, int flags,
+                  void* stream_v) {
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    const int es = elem_bytes(dtype);
+    if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
+    if (op != DT_SUM) return fail(DT_ERR_UNSUPPORTED, "only SUM is supported (as in the reference)");
+    if (count > 0 && (in == nullptr || out == nullptr)) return fail(DT_ERR_INVALID, "null buffer");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    const bool storage = (flags & DT_ACCUM_STORAGE) != 0;
+    if (c->same_device) {
+        return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
+            const char* ins[kMaxRanks];
+            char* outs[kMaxRanks];
+            int nout = 0;
+            for (int r = 0; r < c->n; ++r) {
+                ins[r] = static_cast<const char*>(all[r].in);
+                bool dup = false;
+                for (int j = 0; j < nout; ++j) dup = dup || outs[j] == all[r].out;
+                if (!dup) outs[nout++] = static_cast<char*>(all[r].out);
+            }
+            if (count == 0) return DT_OK;
+            return local_reduce(c->n, ins, outs, nout, count, dtype, flags, st0, s.dev, s.num_sms);
+        });
+    }
+    DT_CUDA(cudaSetDevice(s.dev));
+    if (c->n == 1) {
+        if (count > 0 && in != out) DT_CUDA(cudaMemcpyAsync(out, in, count * es, cudaMemcpyDeviceToDevice, stream));
+        return DT_OK;
+    }
+    ReduceArgs a{};
+    const char* ins[kMaxRanks];
+    char* outs[kMaxRanks];
+    st = resolve_peers(c, rank, in, count * es, out, count * es, ins, outs);
+    if (st != DT_OK) return st;
+    const uint32_t epoch = ++s.epoch;
+    a.sig = make_sig(c, rank);
+    a.bar_start = 2 * epoch - 1;
+    a.bar_end = 2 * epoch;
+    a.n = c->n;
+    const int pv = 16 / es;
+    bool vec_ok = true;
+    for (int r = 0; r < c->n; ++r) {
+        a.in[r] = ins[r];
+        vec_ok = vec_ok && aligned16(ins[r]) && aligned16(outs[r]);
+    }
+    int algo = flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT);
+    if (algo == 0) algo = (count * es <= static_cast<size_t>(256) * 1024) ? DT_ALGO_ONESHOT : DT_ALGO_TWOSHOT;
+    if (in == out) algo = DT_ALGO_TWOSHOT;  // one-shot would overwrite inputs peers still read
+    if (algo == DT_ALGO_ONESHOT) {
+        a.out[0] = outs[rank];
+        a.nout = 1;
+        set_ranges(a, 0, static_cast<int64_t>(count), pv, vec_ok);
+    } else {
+        // chunk c of the vectors belongs to rank c; the element tail belongs to the last rank
+        const int64_t nvec = vec_ok ? static_cast<int64_t>(count) / pv : 0;
+        a.nout = c->n;
+        for (int j = 0; j < c->n; ++j) a.out[j] = outs[(rank + 1 + j) % c->n];
+        if (vec_ok) {
+            a.vlo = nvec * rank / c->n;
+            a.vhi = nvec * (rank + 1) / c->n;
+            a.slo = a.shi = 0;
+            if (rank == c->n - 1) {
+                a.slo = nvec * pv;
+                a.shi = static_cast<int64_t>(count);
+            }
+        } else {
+            a.vlo = a.vhi = 0;
+            a.slo = static_cast<int64_t>(count) * rank / c->n;
+            a.shi = static_cast<int64_t>(count) * (rank + 1) / c->n;
+        }
+    }
+    // grid from sizes every rank shares (vec_ok is computed from every rank's pointers)
+    int64_t want;
+    if (algo == DT_ALGO_ONESHOT) {
+        want = vec_ok ? reduce_want_blocks(static_cast<int64_t>(count) / pv, pv, c->n)
+                      : reduce_want_blocks(0, static_cast<int64_t>(count), c->n);
+    } else {
+        const int64_t nvec = static_cast<int64_t>(count) / pv;
+        want = vec_ok ? reduce_want_blocks((nvec + c->n - 1) / c->n, pv, c->n)
+                      : reduce_want_blocks(0, (static_cast<int64_t>(count) + c->n - 1) / c->n, c->n);
+    }
+    return launch_reduce<true>(a, dtype, storage, s.dev, s.num_sms, stream, want);
+}
+
+int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t out_count, int dtype, int op, int flags,
+                      void* stream_v) {
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    const int es = elem_bytes(dtype);
+    if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
+    if (op != DT_SUM) return fail(DT_ERR_UNSUPPORTED, "only SUM is supported (as in the reference)");
+    if (out_count > 0 && (in == nullptr || out == nullptr)) return fail(DT_ERR_INVALID, "null buffer");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    const size_t in_count = out_count * static_cast<size_t>(c->n);
+    if (c->same_device) {
+        return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
+            if (out_count == 0) return DT_OK;
+            const char* ins[kMaxRanks];
+            for (int r = 0; r < c->n; ++r) ins[r] = static_cast<const char*>(all[r].in);
+            for (int k = 0; k < c->n; ++k) {
+                const char* shifted[kMaxRanks];
+                for (int r = 0; r < c->n; ++r) shifted[r] = ins[r] + static_cast<size_t>(k) * out_count * es;
+                char* o = static_cast<char*>(all[k].out);
+                int rc = local_reduce(c->n, shifted, &o, 1, out_count, dtype, flags, st0, s.dev, s.num_sms);
+                if (rc != DT_OK) return rc;
+            }
+            return DT_OK;
+        });
+    }
+    DT_CUDA(cudaSetDevice(s.dev));
+    if (c->n == 1) {
+        if (out_count > 0 && in != out) DT_CUDA(cudaMemcpyAsync(out, in, out_count * es, cudaMemcpyDeviceToDevice, stream));
+        return DT_OK;
+    }
+    const char* ins[kMaxRanks];
+    char* outs[kMaxRanks];
+    st = resolve_peers(c, rank, in, in_count * es, out, out_count * es, ins, outs);
+    if (st != DT_OK) return st;
+    ReduceArgs a{};
+    const uint32_t epoch = ++s.epoch;
+    a.sig = make_sig(c, rank);
+    a.bar_start = 2 * epoch - 1;
+    a.bar_end = 2 * epoch;
+    a.n = c->n;
+    const int pv = 16 / es;
+    // vector path decided from every rank's pointers and the shared chunk size, so all ranks agree
+    bool vec_ok = static_cast<int64_t>(out_count) % pv == 0;
+    for (int r = 0; r < c->n; ++r) {
+        a.in[r] = ins[r];
+        vec_ok = vec_ok && aligned16(ins[r]) && aligned16(outs[r]);
+    }
+    a.out[0] = outs[rank];
+    a.nout = 1;
+    const int64_t lo = static_cast<int64_t>(out_count) * rank;
+    a.out_shift = lo;
+    set_ranges(a, lo, lo + static_cast<int64_t>(out_count), pv, vec_ok);
+    const int64_t want = vec_ok ? reduce_want_blocks(static_cast<int64_t>(out_count) / pv, 0, c->n)
+                                : reduce_want_blocks(0, static_cast<int64_t>(out_count), c->n);
+    return launch_reduce<true>(a, dtype, (flags & DT_ACCUM_STORAGE) != 0, s.dev, s.num_sms, stream, want);
+}
+
+// ---- all-gather -------------------------------------------------------------------------------------------
+
+int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
+                  size_t inner_bytes, void* stream_v) {
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    if (lens == nullptr) return fail(DT_ERR_INVALID, "null lens");
+    int64_t total = 0, off[kMaxRanks];
+    for (int r = 0; r < c->n; ++r) {
+        if (lens[r] < 0) return fail(DT_ERR_INVALID, "negative shard length");
+        off[r] = total;
+        total += lens[r];
+    }
+    const size_t in_bytes = outer * static_cast<size_t>(lens[rank]) * inner_bytes;
+    const size_t out_bytes = outer * static_cast<size_t>(total) * inner_bytes;
+    if ((in_bytes > 0 && in == nullptr) || (out_bytes > 0 && out == nullptr)) return fail(DT_ERR_INVALID, "null buffer");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    if (c->same_device) {
+        return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
+            const void* ins[kMaxRanks];
+            void* outs[kMaxRanks];
+            int nout = 0;
+            for (int r = 0; r < c->n; ++r) {
+                ins[r] = all[r].in;
+                bool dup = false;
+                for (int j = 0; j < nout; ++j) dup = dup || outs[j] == all[r].out;
+                if (!dup) outs[nout++] = all[r].out;
+            }
+            for (int j = 0; j < nout; ++j) {
+                int rc = dt_local_all_gather(c->n, ins, outs[j], outer, lens, inner_bytes, st0);
+                if (rc != DT_OK) return rc;
+            }
+            return DT_OK;
+        });
+    }
+    DT_CUDA(cudaSetDevice(s.dev));
+    if (c->n == 1) {
+        if (out_bytes > 0 && in != out) DT_CUDA(cudaMemcpyAsync(out, in, out_bytes, cudaMemcpyDeviceToDevice, stream));
+        return DT_OK;
+    }
+    const char* ins[kMaxRanks];
+    char* outs[kMaxRanks];
+    st = resolve_peers(c, rank, in, in_bytes, out, out_bytes, ins, outs);
+    if (st != DT_OK) return st;
+    CopyArgs<kMaxRanks> a{};
+    const uint32_t epoch = ++s.epoch;
+    a.sig = make_sig(c, rank);
+    a.bar_start = 2 * epoch - 1;
+    a.bar_end = 2 * epoch;
+    a.nseg = c->n;
+    for (int j = 0; j < c->n; ++j) {
+        const int k = (rank + 1 + j) % c->n;  // destinations in rotated order, own output last
+        Seg& sg = a.seg[j];
+        sg.src = static_cast<const char*>(in);
+        sg.dst = outs[k] + static_cast<size_t>(off[rank]) * inner_bytes;
+        sg.run = lens[rank] * static_cast<int64_t>(inner_bytes);
+        sg.cnt[0] = sg.cnt[1] = 1;
+        sg.cnt[2] = static_cast<int64_t>(outer);
+        sg.ss[2] = sg.run;
+        sg.ds[2] = total * static_cast<int64_t>(inner_bytes);
+        if (sg.run == 0 || outer == 0) {
+            sg.run = 0;
+            sg.cnt[2] = 1;
+        }
+    }
+    int64_t max_len = 0;
+    for (int r = 0; r < c->n; ++r) max_len = std::max(max_len, lens[r]);
+    const int64_t want = copy_want_blocks(max_len * static_cast<int64_t>(inner_bytes), static_cast<int64_t>(outer), c->n);
+    return launch_copy<kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+}
+
+// ---- all-to-all -------------------------------------------------------------------------------------------
+
+int dt_all_to_all(dt_comm* c, int rank, const void* in, void* out, int ndim, const int64_t* in_shape, int src_dim,
+                  int dst_dim, const int64_t* src_lens, size_t elem_b, void* stream_v) {
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    A2AGeom g{};
+    st = a2a_geom(c->n, ndim, in_shape, src_dim, dst_dim, src_lens, elem_b, &g);
+    if (st != DT_OK) return st;
+    if (in_shape[src_dim] != src_lens[rank]) return fail(DT_ERR_INVALID, "a2a: in_shape[src_dim] != src_lens[rank]");
+    int64_t split[kMaxRanks], doff[kMaxRanks], soff[kMaxRanks];
+    shard_sizes(g.D, c->n, split);
+    int64_t acc = 0;
+    for (int k = 0; k < c->n; ++k) {
+        doff[k] = acc;
+        acc += split[k];
+    }
+    acc = 0;
+    for (int r = 0; r < c->n; ++r) {
+        soff[r] = acc;
+        acc += src_lens[r];
+    }
+    const int64_t in_elems = g.d0 * g.dmid * g.d2 * g.D * src_lens[rank];
+    const int64_t out_elems = g.d0 * g.dmid * g.d2 * g.A * split[rank];
+    if ((in_elems > 0 && in == nullptr) || (out_elems > 0 && out == nullptr)) return fail(DT_ERR_INVALID, "null buffer");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    if (c->same_device) {
+        std::vector<int64_t> shape(in_shape, in_shape + ndim);
+        std::vector<int64_t> lens(src_lens, src_lens + c->n);
+        return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
+            const void* ins[kMaxRanks];
+            void* outs[kMaxRanks];
+            for (int r = 0; r < c->n; ++r) {
+                ins[r] = all[r].in;
+                outs[r] = all[r].out;
+            }
+            return dt_local_all_to_all(c->n, ins, outs, ndim, shape.data(), src_dim, dst_dim, lens.data(), elem_b, st0);
+        });
+    }
+    DT_CUDA(cudaSetDevice(s.dev));
+    if (c->n == 1) {
+        if (in_elems > 0 && in != out) DT_CUDA(cudaMemcpyAsync(out, in, in_elems * elem_b, cudaMemcpyDeviceToDevice, stream));
+        return DT_OK;
+    }
+    const char* ins[kMaxRanks];
+    char* outs[kMaxRanks];
+    st = resolve_peers(c, rank, in, in_elems * elem_b, out, out_elems * elem_b, ins, outs);
+    if (st != DT_OK) return st;
+    CopyArgs<kMaxRanks> a{};
+    const uint32_t epoch = ++s.epoch;
+    a.sig = make_sig(c, rank);
+    a.bar_start = 2 * epoch - 1;
+    a.bar_end = 2 * epoch;
+    a.nseg = c->n;
+    for (int j = 0; j < c->n; ++j) {
+        const int k = (rank + 1 + j) % c->n;
+        a.seg[j] = a2a_seg(g, static_cast<const char*>(in), outs[k], src_lens[rank], soff[rank], split[k], doff[k]);
+    }
+    int64_t max_l = 0;
+    for (int r = 0; r < c->n; ++r) max_l = std::max(max_l, src_lens[r]);
+    const int64_t max_k = split[0];
+    const int64_t run = (g.src_first ? max_k : max_l) * g.d2 * g.es;
+    const int64_t rows = g.d0 * g.dmid * (g.src_first ? max_l : max_k);
+    const int64_t want = copy_want_blocks(run, rows, c->n);
+    return launch_copy<kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+}
+
+int dt_barrier(dt_comm* c, int rank, void* stream_v) {
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    if (c->same_device) {
+        return same_device_call(c, rank, nullptr, nullptr, stream, [](const Slot*, cudaStream_t) { return DT_OK; });
+    }
+    if (c->n == 1) return DT_OK;
+    DT_CUDA(cudaSetDevice(s.dev));
+    if (!c->multiprocess) {
+        // peers must have launched up to the same epoch; nothing to exchange but the rendezvous keeps the
+        // host-side generation counters of the ranks in step with the reference's barrier semantics.
+    }
+    const uint32_t epoch = ++s.epoch;
+    k_barrier<<<1, 32, 0, stream>>>(make_sig(c, rank), 2 * epoch - 1, 2 * epoch);
+    return launch_check("k_barrier");
+}
+
+// ---- same-device kernels ----------------------------------------------------------------------------------
+
+int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, int dtype, int flags, void* stream) {
+    if (n < 1 || n > kMaxRanks || ins == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    if (elem_bytes(dtype) == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
+    if (count == 0) return DT_OK;
+    if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
+    for (int r = 0; r < n; ++r)
+        if (ins[r] == nullptr) return fail(DT_ERR_INVALID, "null input");
+    int dev = 0, sms = 0;
+    int st = current_device_sms(&dev, &sms);
+    if (st != DT_OK) return st;
+    const char* in_c[kMaxRanks];
+    for (int r = 0; r < n; ++r) in_c[r] = static_cast<const char*>(ins[r]);
+    char* o = static_cast<char*>(out);
+    return local_reduce(n, in_c, &o, 1, count, dtype, flags, static_cast<cudaStream_t>(stream), dev, sms);
+}
+
+int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, size_t out_count, int dtype, int flags,
+                            void* stream) {
+    if (n < 1 || n > kMaxRanks || ins == nullptr || outs == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    const int es = elem_bytes(dtype);
+    if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
+    if (out_count == 0) return DT_OK;
+    for (int r = 0; r < n; ++r)
+        if (ins[r] == nullptr || outs[r] == nullptr) return fail(DT_ERR_INVALID, "null buffer");
+    int dev = 0, sms = 0;
+    int st = current_device_sms(&dev, &sms);
+    if (st != DT_OK) return st;
+    for (int k = 0; k < n; ++k) {
+        const char* shifted[kMaxRanks];
+        for (int r = 0; r < n; ++r) shifted[r] = static_cast<const char*>(ins[r]) + static_cast<size_t>(k) * out_count * es;
+        char* o = static_cast<char*>(outs[k]);
+        st = local_reduce(n, shifted, &o, 1, out_count, dtype, flags, static_cast<cudaStream_t>(stream), dev, sms);
+        if (st != DT_OK) return st;
+    }
+    return DT_OK;
+}
+
+int dt_local_all_gather(int n, const void* const* ins, void* out, size_t outer, const int64_t* lens, size_t inner_bytes,
+                        void* stream) {
+    if (n < 1 || n > kMaxRanks || ins == nullptr || lens == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    int64_t total = 0, off[kMaxRanks];
+    for (int r = 0; r < n; ++r) {
+        if (lens[r] < 0) return fail(DT_ERR_INVALID, "negative shard length");
+        off[r] = total;
+        total += lens[r];
+    }
+    if (outer * static_cast<size_t>(total) * inner_bytes == 0) return DT_OK;
+    if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
+    int dev = 0, sms = 0;
+    int st = current_device_sms(&dev, &sms);
+    if (st != DT_OK) return st;
+    CopyArgs<kMaxRanks> a{};
+    a.nseg = n;
+    for (int r = 0; r < n; ++r) {
+        Seg& sg = a.seg[r];
+        sg.src = static_cast<const char*>(ins[r]);
+        sg.dst = static_cast<char*>(out) + static_cast<size_t>(off[r]) * inner_bytes;
+        sg.run = lens[r] * static_cast<int64_t>(inner_bytes);
+        sg.cnt[0] = sg.cnt[1] = 1;
+        sg.cnt[2] = static_cast<int64_t>(outer);
+        sg.ss[2] = sg.run;
+        sg.ds[2] = total * static_cast<int64_t>(inner_bytes);
+        if (sg.run == 0) {
+            sg.cnt[2] = 1;
+        } else if (sg.src == nullptr) {
+            return fail(DT_ERR_INVALID, "null input");
+        }
+    }
+    return launch_copy<kMaxRanks, false>(a, dev, sms, static_cast<cudaStream_t>(stream));
+}
+
+int dt_local_all_to_all(int n, const void* const* ins, void* const* outs, int ndim, const int64_t* in_shape,
+                        int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_b, void* stream) {
+    if (n < 1 || n > kMaxRanks || ins == nullptr || outs == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    A2AGeom g{};
+    int st = a2a_geom(n, ndim, in_shape, src_dim, dst_dim, src_lens, elem_b, &g);
+    if (st != DT_OK) return st;
+    int64_t split[kMaxRanks], doff[kMaxRanks], soff[kMaxRanks];
+    shard_sizes(g.D, n, split);
+    int64_t acc = 0;
+    for (int k = 0; k < n; ++k) {
+        doff[k] = acc;
+        acc += split[k];
+    }
+    acc = 0;
+    for (int r = 0; r < n; ++r) {
+        soff[r] = acc;
+        acc += src_lens[r];
+    }
+    for (int r = 0; r < n; ++r)
+        if ((src_lens[r] > 0 && ins[r] == nullptr) || outs[r] == nullptr) return fail(DT_ERR_INVALID, "null buffer");
+    int dev = 0, sms = 0;
+    st = current_device_sms(&dev, &sms);
+    if (st != DT_OK) return st;
+    CopyArgs<kMaxRanks * kMaxRanks> a{};
+    a.nseg = n * n;
+    // interleave destinations: segment index j*n + i moves source i -> destination (i + j) % n
+    for (int j = 0; j < n; ++j)
+        for (int i = 0; i < n; ++i) {
+            const int k = (i + j) % n;
+            a.seg[j * n + i] = a2a_seg(g, static_cast<const char*>(ins[i]), static_cast<char*>(outs[k]), src_lens[i],
+                                       soff[i], split[k], doff[k]);
+        }
+    return launch_copy<kMaxRanks * kMaxRanks, false>(a, dev, sms, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,358 @@
+// Device code of the redistribute collectives: cross-GPU block barriers, the rank-ordered reduction family
+// (one-shot / two-shot all-reduce, reduce-scatter, same-device reduce) and the segment-copy engine (all-gather
+// with the concat fused, all-to-all with the shard-dim pack fused).
+//
+// Everything here is data movement plus an elementwise add, so it is bound by HBM (local buffers) or by
+// NVLink (peer buffers): 16-byte vector loads and stores, several independent vectors in flight per thread,
+// grids sized to the SM count. Tensor cores are not involved.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dtb {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxBlocks = 1024;  // rows of the per-rank flag array: one row of kMaxRanks flags per block index
+constexpr int kThreads = 512;     // threads per block of every kernel
+constexpr int kErrTimeout = 3;    // == DT_ERR_TIMEOUT
+
+// ------------------------------------------------------------------------------------------------------------
+// Memory-model primitives (PTX ISA: st.release / ld.acquire at system scope, %globaltimer).
+// ------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Signals of one rank: flags[r] is rank r's flag array as addressed from this GPU (a peer pointer for r !=
+// rank). Row b, column s of rank r's array holds the last barrier value block b of rank s announced to r.
+struct SignalCtx {
+    uint32_t* flags[kMaxRanks];
+    int* err;  // this rank's error word (host-mapped)
+    int rank;
+    int n;
+    uint64_t timeout_ns;
+};
+
+// Barrier of block blockIdx.x across all ranks: every prior memory operation of this block (loads of peer
+// inputs, stores into peer outputs) is ordered before the announcement, and nothing after the barrier starts
+// before every rank's block blockIdx.x has announced `value`. Values only grow (two per collective), so flags
+// are never reset; comparisons are wrap-safe. A wait that outlives timeout_ns records kErrTimeout in the
+// error word and the block gives up (returns false) instead of spinning on.
+__device__ __forceinline__ bool block_barrier(const SignalCtx& s, uint32_t value) {
+    __syncthreads();
+    bool ok = true;
+    if (threadIdx.x < s.n) {
+        __threadfence_system();
+        st_release_sys(s.flags[threadIdx.x] + blockIdx.x * kMaxRanks + s.rank, value);
+        const uint32_t* mine = s.flags[s.rank] + blockIdx.x * kMaxRanks + threadIdx.x;
+        uint64_t start = 0;
+        uint32_t spins = 0;
+        while (static_cast<int32_t>(ld_acquire_sys(mine) - value) < 0) {
+            if ((++spins & 31u) == 0) {
+                const uint64_t now = global_timer_ns();
+                if (start == 0) {
+                    start = now;
+                } else if (now - start > s.timeout_ns) {
+                    *reinterpret_cast<volatile int*>(s.err) = kErrTimeout;
+                    ok = false;
+                    break;
+                }
+            }
+        }
+    }
+    return __syncthreads_and(ok) != 0;
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Element types. A 16-byte vector holds kPerVec elements; arithmetic is fp32.
+// ------------------------------------------------------------------------------------------------------------
+template <int DT>
+struct Elem;
+
+template <>
+struct Elem<0> {  // fp32
+    static constexpr int kPerVec = 4;
+    static constexpr int kBytes = 4;
+    __device__ static __forceinline__ void unpack(const uint4& v, float (&f)[4]) {
+        f[0] = __uint_as_float(v.x);
+        f[1] = __uint_as_float(v.y);
+        f[2] = __uint_as_float(v.z);
+        f[3] = __uint_as_float(v.w);
+    }
+    __device__ static __forceinline__ uint4 pack(const float (&f)[4]) {
+        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+    }
+    __device__ static __forceinline__ float round_storage(float x) { return x; }
+    __device__ static __forceinline__ float load1(const char* p) { return *reinterpret_cast<const float*>(p); }
+    __device__ static __forceinline__ void store1(char* p, float x) { *reinterpret_cast<float*>(p) = x; }
+};
+
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+__device__ __forceinline__ uint32_t float_to_bf16_bits(float x) {
+    return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
+}
+
+template <>
+struct Elem<1> {  // bf16
+    static constexpr int kPerVec = 8;
+    static constexpr int kBytes = 2;
+    __device__ static __forceinline__ void unpack(const uint4& v, float (&f)[8]) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+    __device__ static __forceinline__ uint4 pack(const float (&f)[8]) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = float_to_bf16_bits(f[2 * i]) | (float_to_bf16_bits(f[2 * i + 1]) << 16);
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __device__ static __forceinline__ float round_storage(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+    __device__ static __forceinline__ float load1(const char* p) {
+        return bf16_bits_to_float(*reinterpret_cast<const uint16_t*>(p));
+    }
+    __device__ static __forceinline__ void store1(char* p, float x) {
+        *reinterpret_cast<uint16_t*>(p) = static_cast<uint16_t>(float_to_bf16_bits(x));
+    }
+};
+
+template <>
+struct Elem<2> {  // fp16
+    static constexpr int kPerVec = 8;
+    static constexpr int kBytes = 2;
+    __device__ static __forceinline__ void unpack(const uint4& v, float (&f)[8]) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] & 0xffffu)));
+            f[2 * i + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] >> 16)));
+        }
+    }
+    __device__ static __forceinline__ uint4 pack(const float (&f)[8]) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = __half_as_ushort(__float2half_rn(f[2 * i]));
+            const uint32_t hi = __half_as_ushort(__float2half_rn(f[2 * i + 1]));
+            w[i] = lo | (hi << 16);
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __device__ static __forceinline__ float round_storage(float x) { return __half2float(__float2half_rn(x)); }
+    __device__ static __forceinline__ float load1(const char* p) {
+        return __half2float(*reinterpret_cast<const __half*>(p));
+    }
+    __device__ static __forceinline__ void store1(char* p, float x) {
+        *reinterpret_cast<__half*>(p) = __float2half_rn(x);
+    }
+};
+
+// ------------------------------------------------------------------------------------------------------------
+// Rank-ordered reduction.
+//   acc = x_0; acc = acc + x_1; ...; acc = acc + x_{n-1}     (fp32 adds in this order; STORAGE rounds each
+//   partial sum to the storage type, reproducing the reference's in-dtype CPU fold bit for bit)
+// One kernel covers: two-shot all-reduce (this rank's chunk, result pushed to every rank's output),
+// one-shot all-reduce (whole buffer, own output), reduce-scatter (own chunk, own output, shifted index),
+// and the same-device reduce (no barrier, all inputs local).
+// ------------------------------------------------------------------------------------------------------------
+struct ReduceArgs {
+    const char* in[kMaxRanks];  // input of rank r (rank order = summation order)
+    char* out[kMaxRanks];       // outputs written with the result, in store order
+    SignalCtx sig;
+    int64_t vlo, vhi;     // 16-byte vector range of the input this launch reduces
+    int64_t slo, shi;     // element range reduced one element at a time (misaligned buffers, tails)
+    int64_t out_shift;    // output element index = input element index - out_shift
+    int n;                // number of inputs
+    int nout;             // number of outputs
+    uint32_t bar_start;   // barrier values (peer mode)
+    uint32_t bar_end;
+};
+
+template <int DT, int NRMAX, bool STORAGE>
+__device__ __forceinline__ void reduce_vectors(const ReduceArgs& a) {
+    using E = Elem<DT>;
+    constexpr int P = E::kPerVec;
+    constexpr int U = NRMAX <= 2 ? 4 : 2;  // independent vectors per thread per iteration
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x * U;
+    const uint4* in[NRMAX];
+#pragma unroll
+    for (int r = 0; r < NRMAX; ++r) in[r] = reinterpret_cast<const uint4*>(a.in[r < a.n ? r : 0]);
+    const int64_t vshift = a.out_shift / P;  // host guarantees out_shift % P == 0 on the vector path
+    for (int64_t base = a.vlo + static_cast<int64_t>(blockIdx.x) * blockDim.x * U; base < a.vhi; base += step) {
+        uint4 x[NRMAX][U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * blockDim.x + threadIdx.x;
+            if (v < a.vhi) {
+#pragma unroll
+                for (int r = 0; r < NRMAX; ++r)
+                    if (r < a.n) x[r][u] = in[r][v];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * blockDim.x + threadIdx.x;
+            if (v < a.vhi) {
+                float acc[P];
+                E::unpack(x[0][u], acc);
+#pragma unroll
+                for (int r = 1; r < NRMAX; ++r) {
+                    if (r < a.n) {
+                        float t[P];
+                        E::unpack(x[r][u], t);
+#pragma unroll
+                        for (int e = 0; e < P; ++e) acc[e] = STORAGE ? E::round_storage(acc[e] + t[e]) : acc[e] + t[e];
+                    }
+                }
+                const uint4 o = E::pack(acc);
+                for (int j = 0; j < a.nout; ++j) reinterpret_cast<uint4*>(a.out[j])[v - vshift] = o;
+            }
+        }
+    }
+}
+
+template <int DT, bool STORAGE>
+__device__ __forceinline__ void reduce_scalars(const ReduceArgs& a) {
+    using E = Elem<DT>;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = a.slo + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.shi; i += step) {
+        float acc = E::load1(a.in[0] + i * E::kBytes);
+        for (int r = 1; r < a.n; ++r) {
+            const float t = E::load1(a.in[r] + i * E::kBytes);
+            acc = STORAGE ? E::round_storage(acc + t) : acc + t;
+        }
+        for (int j = 0; j < a.nout; ++j) E::store1(a.out[j] + (i - a.out_shift) * E::kBytes, acc);
+    }
+}
+
+template <int DT, int NRMAX, bool STORAGE, bool BARRIER>
+__global__ void __launch_bounds__(kThreads) k_reduce(const __grid_constant__ ReduceArgs a) {
+    if (BARRIER && !block_barrier(a.sig, a.bar_start)) return;
+    reduce_vectors<DT, NRMAX, STORAGE>(a);
+    reduce_scalars<DT, STORAGE>(a);
+    if (BARRIER) block_barrier(a.sig, a.bar_end);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Segment-copy engine. A segment set moves rows of `run` contiguous bytes; rows are indexed by (i0, i1, i2)
+// with independent source and destination byte strides. All-gather along any dim and the all-to-all pack
+// and concat are all such sets: the strided read of the shard-dim slice and the placement at the concat
+// offset happen inside the copy, so no separate contiguous() or concat pass touches HBM.
+// Work item = one segment of up to kSegBytes of one row, copied by one warp (16-byte vectors when VW = 16).
+// Items of different destinations are interleaved so every peer link is busy at once.
+// ------------------------------------------------------------------------------------------------------------
+struct Seg {
+    const char* src;
+    char* dst;
+    int64_t run;       // bytes per row
+    int64_t cnt[3];    // row index extents (i0, i1, i2)
+    int64_t ss[3];     // source byte strides
+    int64_t ds[3];     // destination byte strides
+    int64_t spr;       // segments per row
+    int64_t items;     // rows * spr
+};
+
+template <int MAXSEG>
+struct CopyArgs {
+    Seg seg[MAXSEG];
+    SignalCtx sig;
+    int64_t max_items;  // max over segs of items
+    int nseg;
+    uint32_t bar_start;
+    uint32_t bar_end;
+};
+
+template <int VW>
+struct VecOf;
+template <>
+struct VecOf<16> { using T = uint4; };
+template <>
+struct VecOf<8> { using T = uint2; };
+template <>
+struct VecOf<4> { using T = uint32_t; };
+template <>
+struct VecOf<2> { using T = uint16_t; };
+template <>
+struct VecOf<1> { using T = uint8_t; };
+
+template <int VW>
+struct CopyGeom {
+    static constexpr int kU = VW >= 8 ? 4 : 8;        // vectors per lane per item
+    static constexpr int kSegBytes = 32 * VW * kU;    // bytes per item
+};
+
+template <int VW, int MAXSEG, bool BARRIER>
+__global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyArgs<MAXSEG> a) {
+    using V = typename VecOf<VW>::T;
+    constexpr int U = CopyGeom<VW>::kU;
+    constexpr int SEG = CopyGeom<VW>::kSegBytes;
+    if (BARRIER && !block_barrier(a.sig, a.bar_start)) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int64_t total = a.max_items * a.nseg;
+    for (int64_t t = warp; t < total; t += nwarps) {
+        const int d = static_cast<int>(t % a.nseg);
+        const int64_t j = t / a.nseg;
+        const Seg& s = a.seg[d];
+        if (j >= s.items) continue;
+        int64_t row = j, sg = 0;
+        if (s.spr != 1) {
+            row = j / s.spr;
+            sg = j - row * s.spr;
+        }
+        int64_t so = sg * SEG, dof = sg * SEG;
+        if (s.cnt[0] == 1 && s.cnt[1] == 1) {
+            so += row * s.ss[2];
+            dof += row * s.ds[2];
+        } else {
+            const int64_t i2 = row % s.cnt[2];
+            const int64_t r01 = row / s.cnt[2];
+            const int64_t i1 = r01 % s.cnt[1];
+            const int64_t i0 = r01 / s.cnt[1];
+            so += i0 * s.ss[0] + i1 * s.ss[1] + i2 * s.ss[2];
+            dof += i0 * s.ds[0] + i1 * s.ds[1] + i2 * s.ds[2];
+        }
+        const int64_t len = min(static_cast<int64_t>(SEG), s.run - sg * SEG);
+        const V* src = reinterpret_cast<const V*>(s.src + so);
+        V* dst = reinterpret_cast<V*>(s.dst + dof);
+        V buf[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t off = static_cast<int64_t>(u * 32 + lane) * VW;
+            if (off < len) buf[u] = src[u * 32 + lane];
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t off = static_cast<int64_t>(u * 32 + lane) * VW;
+            if (off < len) dst[u * 32 + lane] = buf[u];
+        }
+    }
+    if (BARRIER) block_barrier(a.sig, a.bar_end);
+}
+
+// Barrier-only kernel (ThreadGroup::Barrier): one block, both phases of the epoch.
+__global__ void k_barrier(const __grid_constant__ SignalCtx s, uint32_t v0, uint32_t v1) {
+    if (block_barrier(s, v0)) block_barrier(s, v1);
+}
+
+}  // namespace dtb

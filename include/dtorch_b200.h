@@ -1,0 +1,190 @@
+/*
+ * dtorch_b200 — C ABI of the B200-native thread-group collectives that execute DTensor redistribution.
+ *
+ * The reference (DTorch) runs every rank of a mesh-dim group as one host thread inside one process and reaches
+ * its collectives through `ThreadGroup` (dtorch/core/communication/thread_group/thread_group.h:29-78), which
+ * forwards to a c10d::Backend picked in the ThreadGroup constructor (thread_group.cc:61-90): ProcessGroupNCCL for
+ * distinct GPUs, ThreadGroupSameDeviceBackend when every rank shares one device. This library is the third
+ * branch: distinct local GPUs in one process (or one process per GPU with IPC-mapped peers), moved by
+ * hand-written sm_100a kernels that load and store peer HBM directly over NVLink / NVSwitch.
+ *
+ * Conventions
+ *   - Every entry point returns dt_status (0 = success) and never aborts the process.
+ *   - Pointers are device pointers on the rank's own GPU unless stated otherwise. `stream` is a cudaStream_t
+ *     passed as void* (NULL = legacy default stream of the rank's device).
+ *   - Collectives are stream-ordered and asynchronous: they enqueue work on `stream` and return.
+ *   - All ranks of a communicator must call the same collectives in the same order (the contract of c10d and
+ *     of the reference's ThreadGroup).
+ *   - Sizes are in elements unless the name ends in _bytes.
+ */
+#ifndef DTORCH_B200_H
+#define DTORCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DT_MAX_RANKS 8
+
+typedef enum dt_status {
+    DT_OK = 0,
+    DT_ERR_INVALID = 1,     /* bad argument: null pointer, rank out of range, size mismatch, unsupported dtype */
+    DT_ERR_CUDA = 2,        /* a CUDA runtime call failed (message in dt_last_error_message) */
+    DT_ERR_TIMEOUT = 3,     /* a host rendezvous or a device-side wait on a peer exceeded the timeout */
+    DT_ERR_PEER = 4,        /* peer access between two devices is unavailable */
+    DT_ERR_UNSUPPORTED = 5, /* valid request this build does not implement (e.g. a non-SUM reduction) */
+    DT_ERR_STATE = 6        /* communicator not ready (multi-process communicator not yet imported) */
+} dt_status;
+
+typedef enum dt_dtype {
+    DT_FLOAT32 = 0,
+    DT_BFLOAT16 = 1,
+    DT_FLOAT16 = 2
+} dt_dtype;
+
+typedef enum dt_redop {
+    DT_SUM = 0 /* c10d::ReduceOp::SUM; the only op the reference asserts (thread_group.cc:212, :283) */
+} dt_redop;
+
+/* Reduction flags (bitwise OR).
+ *   DT_ACCUM_FP32     accumulate in fp32 in rank order 0..n-1, round to the storage type once (default).
+ *   DT_ACCUM_STORAGE  round to the storage type after every add, which is what the reference's CPU fold
+ *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:224-228);
+ *                     bit-identical to it. For fp32 both modes are the same left fold.
+ *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size. */
+#define DT_ACCUM_FP32 0x0
+#define DT_ACCUM_STORAGE 0x1
+#define DT_ALGO_AUTO 0x00
+#define DT_ALGO_ONESHOT 0x10
+#define DT_ALGO_TWOSHOT 0x20
+
+typedef struct dt_comm dt_comm;
+
+/* ---- library ---------------------------------------------------------------------------------------------- */
+
+/* Human-readable name of a status code. */
+const char* dt_status_string(int status);
+
+/* Detail of the last failure on the calling host thread ("" if none). */
+const char* dt_last_error_message(void);
+
+/* ABI version, (major << 16) | minor. */
+int dt_version(void);
+
+/* ---- communicator ------------------------------------------------------------------------------------------ */
+
+/* Single-process communicator over `nranks` ranks, rank r on CUDA device cuda_devices[r].
+ * Replaces the c10d backend construction in ThreadGroup::ThreadGroup (thread_group.cc:61-90) for kGpu with
+ * distinct devices; all ranks of the group live in this process, as in DTorch's single-controller runtime.
+ * Enables peer access between every ordered pair of distinct devices and allocates, per rank, a signal slab
+ * (epoch flags for device-side barriers) plus `heap_bytes` of symmetric heap.
+ * If every rank names the same device, the communicator runs in same-device mode: the equivalent of
+ * ThreadGroupSameDeviceBackend (thread_group_same_device_backend.cc:71-360) — each collective rendezvouses the
+ * rank threads on the host and one kernel does the whole collective on that device. */
+int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_comm** out);
+
+/* Multi-process communicator: this process holds rank `rank` only, on device `cuda_device`.
+ * Peers become reachable after dt_comm_export on every rank and dt_comm_import of all handles. */
+int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes, dt_comm** out);
+
+/* Size of the opaque handle dt_comm_export writes. */
+size_t dt_comm_handle_bytes(void);
+
+/* Write this rank's IPC handle (signal slab + heap) into `handle` (dt_comm_handle_bytes() bytes). */
+int dt_comm_export(dt_comm* comm, void* handle);
+
+/* Map every peer's slab: `handles` holds nranks handles in rank order (this rank's own entry is ignored). */
+int dt_comm_import(dt_comm* comm, const void* handles);
+
+/* Release slabs, mappings and events. Waits for the communicator's outstanding work on its devices. */
+int dt_comm_destroy(dt_comm* comm);
+
+/* Number of ranks, and whether the communicator is in same-device mode (1) or peer mode (0). */
+int dt_comm_size(const dt_comm* comm);
+int dt_comm_same_device(const dt_comm* comm);
+
+/* Base and size of rank `rank`'s symmetric heap. Buffers placed at the same offset on every rank are reached
+ * by peers without a host rendezvous; in a multi-process communicator every buffer a collective reads or
+ * writes on a peer must live in the heap. */
+int dt_comm_heap(dt_comm* comm, int rank, void** base, size_t* bytes);
+
+/* Device-side wait limit for peers, in milliseconds. Default: DTORCH_COMM_TIMEOUT_SECOND * 1000 (the
+ * reference's knob, global_option.cc:20-27, default 600 s). A wait that runs out records DT_ERR_TIMEOUT, the
+ * kernel returns, and dt_comm_error reports it; the GPU context stays usable. */
+int dt_comm_set_timeout_ms(dt_comm* comm, int64_t ms);
+
+/* Sticky device-side error of rank `rank` (DT_OK or DT_ERR_TIMEOUT). Reads host-mapped memory and does not
+ * synchronize; call after the stream has been synchronized to see errors from finished work.
+ * dt_comm_clear_error resets it. */
+int dt_comm_error(dt_comm* comm, int rank);
+int dt_comm_clear_error(dt_comm* comm, int rank);
+
+/* ---- collectives (called by each rank with its own rank index) ---------------------------------------------- */
+
+/* Partial -> Replicate. out[i] = sum over ranks r = 0..n-1 (in that order) of in_r[i], `count` elements.
+ * Replaces ThreadGroup::AllReduce (thread_group.cc:127-141); `in` is not modified (the reference clones it
+ * first, :136). in == out is allowed. */
+int dt_all_reduce(dt_comm* comm, int rank, const void* in, void* out, size_t count, int dtype, int op, int flags,
+                  void* stream);
+
+/* Partial -> Shard(0). out = rows [rank*out_count, (rank+1)*out_count) of the rank-order sum of every rank's
+ * `in` (nranks * out_count elements). Replaces ThreadGroup::ReduceScatterTensor (thread_group.cc:192-209),
+ * which requires dim 0 divisible by the group size (:195). Out of place: no input is modified. */
+int dt_reduce_scatter(dt_comm* comm, int rank, const void* in, void* out, size_t out_count, int dtype, int op,
+                      int flags, void* stream);
+
+/* Shard(d) -> Replicate. Every rank's input is [outer, lens[rank], inner] (inner in bytes: product of the
+ * dims after d times the element size); out is [outer, sum(lens), inner], shards concatenated in rank order
+ * along d. Covers ThreadGroup::EqualShapeAllGatherIntoTensor (:151-166, d = 0, even), AllGather (:168-171,
+ * any d, uneven lens) and AllGatherIntoVec + concat; the concat is fused into the peer stores. */
+int dt_all_gather(dt_comm* comm, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
+                  size_t inner_bytes, void* stream);
+
+/* Shard(src_dim) -> Shard(dst_dim). `in` is this rank's contiguous local tensor of shape in_shape[0..ndim-1]
+ * (in_shape[src_dim] == src_lens[rank]); src_lens[r] is rank r's extent along src_dim. The dst_dim extent D is
+ * split with the reference's rule (first D % n ranks get one more), chunk k goes to rank k, and `out` is
+ * rank's chunk from every peer concatenated along src_dim in rank order: shape in_shape with
+ * [src_dim] = sum(src_lens) and [dst_dim] = split(D)[rank]. Replaces ThreadGroup::AllToAll
+ * (thread_group.cc:211-241): the per-chunk .contiguous() pack and the final concat are fused into the peer
+ * stores. */
+int dt_all_to_all(dt_comm* comm, int rank, const void* in, void* out, int ndim, const int64_t* in_shape,
+                  int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_bytes, void* stream);
+
+/* Device-side barrier of all ranks on their streams. Replaces ThreadGroup::Barrier (thread_group.cc:118-125). */
+int dt_barrier(dt_comm* comm, int rank, void* stream);
+
+/* ---- same-device kernels: all n ranks' buffers on the current device, one launch ------------------------- */
+/* These are the kernels a same-device communicator launches; they are exported so a caller that already holds
+ * every rank's buffer (the 1-GPU emulation mode, DTORCH_DTENSOR_IN_SAME_DEVICE in the reference) can use them
+ * directly. `ins`/`outs` are host arrays of n device pointers. */
+
+/* out = rank-order sum of ins[0..n-1] (the fold of thread_group_same_device_backend.cc:224-228). */
+int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, int dtype, int flags, void* stream);
+
+/* outs[r] = rows [r*out_count, (r+1)*out_count) of the rank-order sum (same-device _reduce_scatter_base,
+ * thread_group_same_device_backend.cc:238-274, without its in-place write into rank 0's input). */
+int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, size_t out_count, int dtype, int flags,
+                            void* stream);
+
+/* out = concat of ins[r] ([outer, lens[r], inner_bytes]) along the middle dim in rank order. */
+int dt_local_all_gather(int n, const void* const* ins, void* out, size_t outer, const int64_t* lens,
+                        size_t inner_bytes, void* stream);
+
+/* outs[k] = concat over r of chunk k (along dst_dim) of ins[r], along src_dim. Shapes as dt_all_to_all, with
+ * ins[r] of shape in_shape except [src_dim] = src_lens[r]. */
+int dt_local_all_to_all(int n, const void* const* ins, void* const* outs, int ndim, const int64_t* in_shape,
+                        int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_bytes, void* stream);
+
+/* ---- instrumentation -------------------------------------------------------------------------------------- */
+
+/* Number of kernels this library has launched on the calling process since load (all threads). */
+uint64_t dt_kernel_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DTORCH_B200_H */

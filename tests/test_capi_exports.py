@@ -1,0 +1,44 @@
+"""CPU: the C-ABI library loads without a GPU and exports every entry point include/dtorch_b200.h declares,
+with the signature table of the Python binding covering exactly those entry points."""
+
+import ctypes
+import os
+import re
+
+from dtorch_b200 import capi
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "dtorch_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\**\s*(dt_[a-z0-9_]+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "dt_all_reduce" in names and "dt_all_to_all" in names and "dt_comm_create" in names
+    assert len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(capi.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_table_matches_header():
+    assert sorted(n for n, _, _ in capi.SIGNATURES) == declared_functions()
+
+
+def test_host_only_calls():
+    L = capi.lib()
+    assert L.dt_version() >> 16 == 1
+    assert L.dt_status_string(capi.DT_ERR_TIMEOUT) == b"timeout waiting for a peer"
+    assert L.dt_comm_handle_bytes() >= 64
+    # invalid arguments are rejected before any CUDA call
+    assert L.dt_comm_create(0, None, 0, None) == capi.DT_ERR_INVALID
+    assert L.dt_all_reduce(None, 0, None, None, 0, 0, 0, 0, None) == capi.DT_ERR_INVALID
+    assert L.dt_local_all_reduce(0, None, None, 0, 0, 0, None) == capi.DT_ERR_INVALID
+    assert L.dt_local_all_reduce(2, None, None, 16, 9, 0, None) == capi.DT_ERR_INVALID

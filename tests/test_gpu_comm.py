@@ -1,0 +1,220 @@
+"""GPU parity of the communicator entry points, called the way the reference calls its ThreadGroup: one host
+thread per rank, each on its own stream (dtorch/tests/test_nccl.cc:27-65).
+
+* same-device communicator: every rank on cuda:0 (the reference's ThreadGroupSameDeviceBackend mode)
+* peer communicator: rank r on cuda:r, kernels moving data through peer HBM (needs >= 2 GPUs)
+* bounded waits: a peer that never arrives ends in DT_ERR_TIMEOUT, not a hang
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from dtorch_b200 import capi
+from oracle.oracle import Restatement, shard_sizes
+from tests.gpu_util import np_raw, run_ranks, to_dev, view_device_memory
+from tests.helpers import DT_CODE, assert_close, golden_cases, raw_from_torch
+
+pytestmark = pytest.mark.gpu
+R = Restatement()
+TD = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def ngpu():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.fixture(autouse=True)
+def _need_gpu():
+    if ngpu() < 1:
+        pytest.skip("no CUDA device")
+
+
+def devices_for(n, mode):
+    if mode == "same":
+        return [0] * n
+    if ngpu() < n:
+        pytest.skip(f"peer mode with {n} ranks needs {n} GPUs")
+    return list(range(n))
+
+
+def run_case(comm, devs, meta, ins, flags=0):
+    """Run one golden case through the communicator; returns per-rank raw outputs."""
+    n = meta["n"]
+    dt = meta["dtype"]
+    op = meta["op"]
+    code = DT_CODE[dt]
+    d_in = [to_dev(a, dt, devs[r]) for r, a in enumerate(ins)]
+    streams = [torch.cuda.Stream(device=devs[r]) for r in range(n)]
+    outs = [None] * n
+
+    def rank_fn(r):
+        with torch.cuda.device(devs[r]):
+            s = streams[r]
+            s.wait_stream(torch.cuda.current_stream(devs[r]))
+            with torch.cuda.stream(s):
+                x = d_in[r]
+                if op == "all_reduce":
+                    o = torch.empty_like(x)
+                    comm.all_reduce(r, x.data_ptr(), o.data_ptr(), x.numel(), code, flags, s.cuda_stream)
+                elif op == "reduce_scatter":
+                    o = torch.empty(x.numel() // n, dtype=x.dtype, device=x.device)
+                    comm.reduce_scatter(r, x.data_ptr(), o.data_ptr(), o.numel(), code, flags, s.cuda_stream)
+                elif op == "all_gather":
+                    dim = meta["dim"]
+                    shp = list(ins[r].shape)
+                    lens = [a.shape[dim] for a in ins]
+                    outer = int(np.prod(shp[:dim], dtype=np.int64))
+                    inner = int(np.prod(shp[dim + 1:], dtype=np.int64)) * ins[r].itemsize
+                    o = torch.empty(outer * sum(lens) * inner // ins[r].itemsize, dtype=x.dtype, device=x.device)
+                    comm.all_gather(r, x.data_ptr(), o.data_ptr(), outer, lens, inner, s.cuda_stream)
+                else:
+                    sd, dd = meta["src_dim"], meta["dst_dim"]
+                    lens = [a.shape[sd] for a in ins]
+                    split = shard_sizes(ins[0].shape[dd], n)
+                    numel = ins[r].size // ins[r].shape[sd] * sum(lens) // ins[r].shape[dd] * split[r]
+                    o = torch.empty(numel, dtype=x.dtype, device=x.device)
+                    comm.all_to_all(r, x.data_ptr(), o.data_ptr(), list(ins[r].shape), sd, dd, lens,
+                                    ins[r].itemsize, s.cuda_stream)
+                outs[r] = o
+            s.synchronize()
+
+    run_ranks(n, rank_fn)
+    return [np_raw(o) for o in outs]
+
+
+@pytest.mark.parametrize("mode", ["same", "peer"])
+@pytest.mark.parametrize("case", golden_cases(), ids=lambda c: c[0])
+def test_comm_golden(case, mode):
+    name, meta, ins, outs = case
+    n, op, dt = meta["n"], meta["op"], meta["dtype"]
+    devs = devices_for(n, mode)
+    comm = capi.Comm(devs)
+    try:
+        comm.set_timeout_ms(20000)
+        reduce_op = op in ("all_reduce", "reduce_scatter")
+        got = run_case(comm, devs, meta, ins, flags=capi.DT_ACCUM_STORAGE if reduce_op else 0)
+        for r in range(n):
+            assert np.array_equal(got[r].reshape(outs[r].shape), outs[r]), (name, r)
+        if reduce_op:
+            # default fp32 accumulation: bit-exact vs the restatement in that mode, within tolerance of the reference
+            got = run_case(comm, devs, meta, ins, flags=0)
+            want = (R.fold_sum(ins, DT_CODE[dt], False) if op == "all_reduce"
+                    else R.reduce_scatter(ins, DT_CODE[dt], False))
+            for r in range(n):
+                w = want if op == "all_reduce" else want[r]
+                assert np.array_equal(got[r], w.reshape(-1)), (name, r)
+                assert_close(got[r], outs[r].reshape(-1), dt)
+        assert comm.error(0) == capi.DT_OK
+    finally:
+        comm.destroy()
+
+
+@pytest.mark.parametrize("algo", [capi.DT_ALGO_ONESHOT, capi.DT_ALGO_TWOSHOT])
+@pytest.mark.parametrize("count", [1, 7, 4096 + 3, (1 << 21) + 9])
+def test_peer_all_reduce_algorithms(algo, count):
+    n = min(ngpu(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    devs = list(range(n))
+    comm = capi.Comm(devs)
+    try:
+        g = torch.Generator().manual_seed(count)
+        host = [torch.randn(count, generator=g).to(torch.bfloat16) for _ in range(n)]
+        d_in = [h.to(f"cuda:{r}") for r, h in enumerate(host)]
+        outs = [torch.empty_like(t) for t in d_in]
+
+        def fn(r):
+            with torch.cuda.device(r):
+                comm.all_reduce(r, d_in[r].data_ptr(), outs[r].data_ptr(), count, capi.DT_BFLOAT16, algo,
+                                torch.cuda.current_stream(r).cuda_stream)
+                torch.cuda.current_stream(r).synchronize()
+
+        for _ in range(3):  # back-to-back calls reuse the flags with growing epochs
+            run_ranks(n, fn)
+        want = R.fold_sum([raw_from_torch(h) for h in host], 1, storage_round=False)
+        for r in range(n):
+            assert np.array_equal(np_raw(outs[r]), want), r
+    finally:
+        comm.destroy()
+
+
+def test_peer_in_place_all_reduce_and_heap_buffers():
+    n = min(ngpu(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    devs = list(range(n))
+    count = (1 << 20) + 16
+    comm = capi.Comm(devs, heap_bytes=8 << 20)
+    try:
+        g = torch.Generator().manual_seed(1)
+        host = [torch.randn(count, generator=g) for _ in range(n)]
+        bufs = []
+        for r in range(n):
+            base, size = comm.heap(r)
+            assert size == 8 << 20
+            t = view_device_memory(base, count, torch.float32, r)
+            t.copy_(host[r].to(f"cuda:{r}"))
+            bufs.append(t)
+        torch.cuda.synchronize()
+
+        def fn(r):
+            with torch.cuda.device(r):
+                # heap buffers: peers are reached by symmetric offset, no host rendezvous; in place
+                comm.all_reduce(r, bufs[r].data_ptr(), bufs[r].data_ptr(), count, capi.DT_FLOAT32, 0,
+                                torch.cuda.current_stream(r).cuda_stream)
+                torch.cuda.current_stream(r).synchronize()
+
+        run_ranks(n, fn)
+        want = R.fold_sum([h.numpy() for h in host], 0, storage_round=False)
+        for r in range(n):
+            assert np.array_equal(bufs[r].cpu().numpy(), want)
+    finally:
+        comm.destroy()
+
+
+def test_peer_device_wait_times_out_cleanly():
+    """Rank 1 never launches: rank 0's barrier kernel gives up after the 1 s limit, records DT_ERR_TIMEOUT
+    in the host-mapped error word and returns; the context stays usable."""
+    if ngpu() < 2:
+        pytest.skip("needs >= 2 GPUs")
+    comm = capi.Comm([0, 1])
+    try:
+        comm.set_timeout_ms(1000)
+        with torch.cuda.device(0):
+            s = torch.cuda.current_stream(0)
+            comm.barrier(0, s.cuda_stream)
+            s.synchronize()
+        assert comm.error(0) == capi.DT_ERR_TIMEOUT
+        x = torch.ones(16, device="cuda:0") * 2
+        assert float(x.sum()) == 32.0  # the GPU still answers
+    finally:
+        comm.destroy()
+
+
+def test_same_device_rendezvous_times_out_cleanly():
+    """One rank thread never arrives: the others get DT_ERR_TIMEOUT from the host rendezvous; no kernel waits."""
+    comm = capi.Comm([0, 0, 0])
+    try:
+        comm.set_timeout_ms(300)
+        x = torch.ones(64, device="cuda:0")
+        o = torch.empty_like(x)
+        errs = []
+
+        def fn(r):
+            if r == 2:
+                return
+            try:
+                comm.all_reduce(r, x.data_ptr(), o.data_ptr(), 64, capi.DT_FLOAT32, 0, 0)
+            except capi.DtError as e:
+                errs.append(e.status)
+
+        run_ranks(3, fn)
+        assert sorted(errs) == [capi.DT_ERR_TIMEOUT, capi.DT_ERR_TIMEOUT]
+        with pytest.raises(capi.DtError) as ei:
+            comm.all_reduce(0, x.data_ptr(), o.data_ptr(), 64, capi.DT_FLOAT32, 0, 0)
+        assert ei.value.status == capi.DT_ERR_STATE  # broken communicator refuses further calls
+    finally:
+        comm.destroy()
