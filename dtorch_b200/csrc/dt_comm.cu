@@ -48,6 +48,21 @@ constexpr size_t kFlagBytes = static_cast<size_t>(kMaxBlocks) * kMaxRanks * size
 constexpr size_t kHeapOffset = 64 * 1024;  // heap starts 64 KiB into the slab (flags first)
 constexpr uint32_t kHandleMagic = 0x44544232u;  // "DTB2"
 
+// Restores the calling thread's current device on scope exit: the CUDA runtime shares the thread's current
+// context with every other runtime in the process (torch included), so entry points must not leak a switch.
+struct DeviceGuard {
+    int prev = -1;
+    DeviceGuard() {
+        if (cudaGetDevice(&prev) != cudaSuccess) {
+            prev = -1;
+            cudaGetLastError();
+        }
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
 int elem_bytes(int dtype) {
     switch (dtype) {
         case DT_FLOAT32: return 4;
@@ -625,6 +640,7 @@ int dt_version(void) { return (1 << 16) | 0; }
 uint64_t dt_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_comm** out) {
+    DeviceGuard device_guard;
     if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
     *out = nullptr;
     if (nranks < 1 || nranks > kMaxRanks || cuda_devices == nullptr) return fail(DT_ERR_INVALID, "nranks must be 1..8");
@@ -695,6 +711,7 @@ int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_co
 }
 
 int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes, dt_comm** out) {
+    DeviceGuard device_guard;
     if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
     *out = nullptr;
     if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks) return fail(DT_ERR_INVALID, "bad rank/nranks");
@@ -721,6 +738,7 @@ int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes
 size_t dt_comm_handle_bytes(void) { return sizeof(IpcHandle); }
 
 int dt_comm_export(dt_comm* c, void* handle) {
+    DeviceGuard device_guard;
     if (c == nullptr || handle == nullptr || !c->multiprocess) return fail(DT_ERR_INVALID, "export needs a multi-process communicator");
     RankState& s = c->r[c->local_rank];
     IpcHandle h{};
@@ -735,6 +753,7 @@ int dt_comm_export(dt_comm* c, void* handle) {
 }
 
 int dt_comm_import(dt_comm* c, const void* handles) {
+    DeviceGuard device_guard;
     if (c == nullptr || handles == nullptr || !c->multiprocess) return fail(DT_ERR_INVALID, "import needs a multi-process communicator");
     const int me = c->local_rank;
     RankState& s = c->r[me];
@@ -757,6 +776,7 @@ int dt_comm_import(dt_comm* c, const void* handles) {
 }
 
 int dt_comm_destroy(dt_comm* c) {
+    DeviceGuard device_guard;
     if (c == nullptr) return DT_OK;
     for (int i = 0; i < kMaxRanks; ++i) {
         RankState& s = c->r[i];
@@ -808,6 +828,7 @@ int dt_comm_clear_error(dt_comm* c, int rank) {
 int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count, int dtype, int op, int flags,
                   void* stream_v) {
     int st = common_checks(c, rank);
+    DeviceGuard device_guard;
     if (st != DT_OK) return st;
     const int es = elem_bytes(dtype);
     if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
@@ -894,6 +915,7 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
 int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t out_count, int dtype, int op, int flags,
                       void* stream_v) {
     int st = common_checks(c, rank);
+    DeviceGuard device_guard;
     if (st != DT_OK) return st;
     const int es = elem_bytes(dtype);
     if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
@@ -953,6 +975,7 @@ int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t ou
 
 int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
                   size_t inner_bytes, void* stream_v) {
+    DeviceGuard device_guard;
     int st = common_checks(c, rank);
     if (st != DT_OK) return st;
     if (lens == nullptr) return fail(DT_ERR_INVALID, "null lens");
@@ -1025,6 +1048,7 @@ int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer,
 
 int dt_all_to_all(dt_comm* c, int rank, const void* in, void* out, int ndim, const int64_t* in_shape, int src_dim,
                   int dst_dim, const int64_t* src_lens, size_t elem_b, void* stream_v) {
+    DeviceGuard device_guard;
     int st = common_checks(c, rank);
     if (st != DT_OK) return st;
     A2AGeom g{};
@@ -1090,6 +1114,7 @@ int dt_all_to_all(dt_comm* c, int rank, const void* in, void* out, int ndim, con
 }
 
 int dt_barrier(dt_comm* c, int rank, void* stream_v) {
+    DeviceGuard device_guard;
     int st = common_checks(c, rank);
     if (st != DT_OK) return st;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_v);

@@ -7,6 +7,7 @@
 
 #include <torch/torch.h>
 
+#include "dtorch/common/debug.h"
 #include "dtorch/common/utilities.h"
 
 namespace dtorch {
@@ -41,6 +42,7 @@ private:
 class Placement {
 public:
     static std::vector<int64_t> GetShardSizeForAllRank(int64_t shapeSize, int64_t numShard) {
+        DDebugAssert(shapeSize >= numShard);  // active in the reference's default build (DTORCH_DEBUG ON)
         std::vector<int64_t> out(static_cast<size_t>(numShard), shapeSize / numShard);
         for (int64_t i = 0; i < shapeSize % numShard; ++i) out[static_cast<size_t>(i)] += 1;
         return out;

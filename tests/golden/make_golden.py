@@ -83,7 +83,7 @@ def main():
     # Shard(i) -> Shard(j) (the reference test's S1<->S0 on (4,8)/(5,9), a Ulysses-shaped case, odd shapes)
     for n, dtype, full, sd, dd in [(2, "float32", (4, 8), 0, 1), (2, "float32", (5, 9), 1, 0),
                                    (2, "float32", (5, 9), 0, 1), (4, "bfloat16", (1, 16, 8, 4), 1, 2),
-                                   (4, "bfloat16", (1, 8, 16, 4), 2, 1), (8, "float16", (2, 11, 13, 3), 2, 0),
+                                   (4, "bfloat16", (1, 8, 16, 4), 2, 1), (8, "float16", (16, 11, 13, 3), 2, 0),
                                    (3, "float32", (6, 7, 5), 0, 2), (8, "bfloat16", (1, 32, 16, 8), 1, 2)]:
         lens = shard_sizes(full[sd], n)
         ins = []

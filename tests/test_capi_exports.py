@@ -42,3 +42,15 @@ def test_host_only_calls():
     assert L.dt_all_reduce(None, 0, None, None, 0, 0, 0, 0, None) == capi.DT_ERR_INVALID
     assert L.dt_local_all_reduce(0, None, None, 0, 0, 0, None) == capi.DT_ERR_INVALID
     assert L.dt_local_all_reduce(2, None, None, 16, 9, 0, None) == capi.DT_ERR_INVALID
+
+
+def test_all_to_all_rejects_dst_extent_below_group():
+    # The reference asserts shapeSize >= numShard in GetShardSizeForAllRank (distributed_spec.cc:203, active in
+    # its default DTORCH_DEBUG build) and CheckValid rejects such placements; the C ABI refuses them too,
+    # before touching the device.
+    L = capi.lib()
+    dummy = capi.ptr_array([16] * 8)
+    shape = capi.i64_array([2, 11, 2, 3])
+    lens = capi.i64_array([2, 2, 2, 2, 2, 1, 1, 1])
+    assert L.dt_local_all_to_all(8, dummy, dummy, 4, shape, 2, 0, lens, 2, None) == capi.DT_ERR_INVALID
+    assert b"dst dim" in L.dt_last_error_message()
