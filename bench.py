@@ -91,73 +91,80 @@ def profile_traffic(key):
 # ---------------------------------------------------------------------------------------------------------
 # Clock sampling during the timed region (NVML; nvidia-smi as fallback)
 # ---------------------------------------------------------------------------------------------------------
+_SAMPLER = r"""
+import sys, time
+import pynvml as nv
+nv.nvmlInit()
+h = nv.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+period = float(sys.argv[2])
+print("max", nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), flush=True)
+while True:
+    try:
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+    except Exception:
+        r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+    print(time.time(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), int(r), flush=True)
+    time.sleep(period)
+"""
+
+
 class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML in a separate process (a sampling thread would
+    compete for the GIL with the launch loop) during the timed region."""
+
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
         "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.002):
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.dev = device_index
         self.period = period_s
-        self.samples = []
-        self.reasons = 0
+        self.proc = None
         self.max_mhz = None
-        self._stop = threading.Event()
-        self._t = None
-        self.ok = False
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-            self.ok = True
-        except Exception:
-            self.nv = None
-
-    def _sample(self):
-        nv = self.nv
-        mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
-        try:
-            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-        except Exception:
-            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
-        self.samples.append(mhz)
-        self.reasons |= int(r)
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self._sample()
-            except Exception:
-                return
-            time.sleep(self.period)
+        self.samples = []
+        self.t0 = self.t1 = 0.0
 
     def __enter__(self):
-        if self.ok:
-            self._t = threading.Thread(target=self._run, daemon=True)
-            self._t.start()
+        import subprocess
+
+        try:
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.dev), str(self.period)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline().split()
+            self.max_mhz = int(first[1]) if len(first) == 2 and first[0] == "max" else None
+            self.proc.stdout.readline()  # one sample taken: the sampler is running
+        except Exception:
+            self.proc = None
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *a):
-        if self.ok:
-            self._stop.set()
-            self._t.join()
-            if not self.samples:
-                try:
-                    self._sample()
-                except Exception:
-                    pass
+        self.t1 = time.time()
+        if self.proc is None:
+            return
+        time.sleep(2 * self.period)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) == 3:
+                self.samples.append((float(f[0]), int(f[1]), int(f[2])))
 
     def summary(self):
-        if not self.ok:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
-        names = [k for k, v in self.REASONS.items() if self.reasons & v and k != "gpu_idle"]
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
-                "reasons": names, "samples": len(self.samples)}
+        if self.proc is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        inside = [s for s in self.samples if self.t0 <= s[0] <= self.t1]
+        if not inside:  # region shorter than one period: the first sample after it
+            after = [s for s in self.samples if s[0] > self.t1]
+            inside = after[:1] or self.samples[-1:]
+        reasons = 0
+        for s in inside:
+            reasons |= s[2]
+        names = [k for k, v in self.REASONS.items() if reasons & v and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median([s[1] for s in inside]), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(inside), "region_s": round(self.t1 - self.t0, 4)}
 
 
 # ---------------------------------------------------------------------------------------------------------
@@ -548,9 +555,11 @@ def run_ours_multi(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    dist.barrier()
     l0 = capi.launch_count()
     with ClockSampler(local_rank) as clk:
+        # ranks start their samplers at different times: line them up after, right before the timed steps
+        dist.barrier()
+        torch.cuda.synchronize()
         ms = time_steps(step, args.steps, stream)
     launches = capi.launch_count() - l0
     dist.barrier()
@@ -636,6 +645,181 @@ def run_ours_multi(args, rank, world, local_rank):
     dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------------------------------------
+# C5: message-size sweep (one JSON line per op / dtype / size; not the driver's single-line contract)
+# ---------------------------------------------------------------------------------------------------------
+def sweep_sizes(lo, hi):
+    return [1 << k for k in range(lo, hi + 1)]
+
+
+def a2a_shape(elems, n):
+    """Per-rank (a, n*b) Shard(0)->Shard(1) with a*b*n = elems and 1024-element rows per (row, destination)."""
+    b = max(1, min(1024, elems // n))
+    a = max(1, elems // (n * b))
+    return a, b
+
+
+def run_sweep_multi(args, rank, world, local_rank):
+    import datetime
+
+    import torch.distributed as dist
+
+    from dtorch_b200 import capi
+
+    n = world
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    max_bytes = 1 << args.sweep_hi
+    comm = capi.Comm.for_rank(n, rank, local_rank, 2 * max_bytes + (4 << 20))
+    handles = [None] * n
+    dist.all_gather_object(handles, comm.export_handle())
+    comm.import_handles(handles)
+    base, _ = comm.heap(rank)
+    stream = torch.cuda.current_stream(dev)
+    ops = args.sweep_ops.split(",")
+    for op in ops:
+        for dtype in ([torch.bfloat16, torch.float32] if op in ("all_reduce", "reduce_scatter") else [torch.bfloat16]):
+            es = torch.tensor([], dtype=dtype).element_size()
+            code = capi.dtype_code(dtype)
+            for S in sweep_sizes(args.sweep_lo, args.sweep_hi):
+                E = S // es
+                if op == "all_reduce":
+                    in_n, out_n = E, E
+                elif op == "reduce_scatter":
+                    E = E // n * n
+                    in_n, out_n = E, E // n
+                elif op == "all_gather":
+                    E = E // n * n
+                    in_n, out_n = E // n, E
+                else:
+                    a, b = a2a_shape(E, n)
+                    in_n = out_n = a * n * b
+                if in_n == 0 or out_n == 0:
+                    continue
+                x = heap_tensor(base, 0, in_n, dtype, dev)
+                y = heap_tensor(base, max_bytes + (2 << 20), out_n, dtype, dev)
+                g = torch.Generator(device=dev).manual_seed(rank)
+                x.copy_((torch.rand(in_n, generator=g, device=dev) * 2 - 1).to(dtype))
+
+                def ours():
+                    st = stream.cuda_stream
+                    if op == "all_reduce":
+                        comm.all_reduce(rank, x.data_ptr(), y.data_ptr(), in_n, code, 0, st)
+                    elif op == "reduce_scatter":
+                        comm.reduce_scatter(rank, x.data_ptr(), y.data_ptr(), out_n, code, 0, st)
+                    elif op == "all_gather":
+                        comm.all_gather(rank, x.data_ptr(), y.data_ptr(), 1, [in_n] * n, es, st)
+                    else:
+                        comm.all_to_all(rank, x.data_ptr(), y.data_ptr(), [a, n * b], 0, 1, [a] * n, es, st)
+
+                xa = torch.empty(in_n, dtype=dtype, device=dev).copy_(x)
+                ya = torch.empty(out_n, dtype=dtype, device=dev)
+
+                def nccl():
+                    if op == "all_reduce":
+                        dist.all_reduce(xa)
+                    elif op == "reduce_scatter":
+                        dist.reduce_scatter_tensor(ya, xa)
+                    elif op == "all_gather":
+                        dist.all_gather_into_tensor(ya, xa)
+                    else:
+                        dist.all_to_all_single(ya, xa)
+
+                res = {}
+                for name, fn in (("ours", ours), ("nccl", nccl)):
+                    for _ in range(3):
+                        fn()
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    t0 = time.perf_counter()
+                    fn()
+                    torch.cuda.synchronize()
+                    one = time.perf_counter() - t0
+                    # every rank must issue the same number of collectives: agree on the max
+                    it_t = torch.tensor([int(min(200, max(5, 0.02 / max(one, 1e-6))))], device=dev)
+                    dist.all_reduce(it_t, op=dist.ReduceOp.MAX)
+                    iters = int(it_t.item())
+                    dist.barrier()
+                    ms = time_steps(fn, iters, stream)
+                    tm = torch.tensor([ms], device=dev)
+                    dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+                    res[name] = float(tm.item())
+                busf = bus_factor(op, n)
+                msg = in_n * es if op != "all_gather" else out_n * es
+                if rank == 0:
+                    print(json.dumps({"sweep": op, "n_gpus": n, "dtype": DT_NAME[dtype], "bytes": msg,
+                                      "ours_ms": round(res["ours"], 5), "nccl_ms": round(res["nccl"], 5),
+                                      "ours_bus_gbs": round(msg * busf / res["ours"] / 1e6, 2),
+                                      "nccl_bus_gbs": round(msg * busf / res["nccl"] / 1e6, 2),
+                                      "device_error": comm.error(rank)}), flush=True)
+                del xa, ya
+    dist.barrier()
+    comm.destroy()
+    dist.destroy_process_group()
+
+
+def run_sweep_single(args):
+    """1 GPU: the same-device kernels for a group of `emul_n` ranks against HBM."""
+    from dtorch_b200 import capi
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream(device=0)
+    n = 8
+    peaks, _ = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    for op in args.sweep_ops.split(","):
+        for dtype in ([torch.bfloat16, torch.float32] if op in ("all_reduce", "reduce_scatter") else [torch.bfloat16]):
+            es = torch.tensor([], dtype=dtype).element_size()
+            code = capi.dtype_code(dtype)
+            for S in sweep_sizes(args.sweep_lo, min(args.sweep_hi, 29)):
+                E = S // es // n * n
+                if E == 0:
+                    continue
+                if op in ("all_reduce", "reduce_scatter"):
+                    ins = [(torch.rand(E, device="cuda:0") * 2 - 1).to(dtype) for _ in range(n)]
+                    outs = [torch.empty(E if op == "all_reduce" else E // n, dtype=dtype, device="cuda:0")
+                            for _ in range(1 if op == "all_reduce" else n)]
+                    hbm_bytes = (n + 1) * E * es
+                    msg = E * es
+                elif op == "all_gather":
+                    ins = [torch.rand(E // n, device="cuda:0").to(dtype) for _ in range(n)]
+                    outs = [torch.empty(E, dtype=dtype, device="cuda:0")]
+                    hbm_bytes = 2 * E * es
+                    msg = E * es
+                else:
+                    a, b = a2a_shape(E, n)
+                    ins = [torch.rand(a * n * b, device="cuda:0").to(dtype) for _ in range(n)]
+                    outs = [torch.empty(a * n * b, dtype=dtype, device="cuda:0") for _ in range(n)]
+                    hbm_bytes = 2 * n * a * n * b * es
+                    msg = a * n * b * es
+                ip = [t.data_ptr() for t in ins]
+                op_ = [t.data_ptr() for t in outs]
+
+                def fn():
+                    st = stream.cuda_stream
+                    if op == "all_reduce":
+                        capi.local_all_reduce(ip, op_[0], E, code, 0, st)
+                    elif op == "reduce_scatter":
+                        capi.local_reduce_scatter(ip, op_, E // n, code, 0, st)
+                    elif op == "all_gather":
+                        capi.local_all_gather(ip, op_[0], 1, [E // n] * n, es, st)
+                    else:
+                        capi.local_all_to_all(ip, op_, [a, n * b], 0, 1, [a] * n, es, st)
+
+                with torch.cuda.stream(stream):
+                    for _ in range(3):
+                        fn()
+                    ms = time_steps(fn, 20, stream)
+                print(json.dumps({"sweep": op, "n_gpus": 1, "group_ranks": n, "dtype": DT_NAME[dtype], "bytes": msg,
+                                  "ours_ms": round(ms, 5),
+                                  "ours_bus_gbs": round(msg * bus_factor(op, n) / ms / 1e6, 2),
+                                  "hbm_gbs": round(hbm_bytes / ms / 1e6, 1),
+                                  "hbm_frac": round(hbm_bytes / ms / 1e6 / hbm, 4)}), flush=True)
+                del ins, outs
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -645,6 +829,10 @@ def main():
     p.add_argument("--op", choices=list(CONFIGS), default="all_reduce")
     p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     p.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end leg (profiling runs)")
+    p.add_argument("--sweep", action="store_true", help="C5 message-size sweep, one JSON line per point")
+    p.add_argument("--sweep-lo", type=int, default=10, help="smallest size, log2 bytes")
+    p.add_argument("--sweep-hi", type=int, default=30, help="largest size, log2 bytes")
+    p.add_argument("--sweep-ops", default="all_reduce,all_gather,reduce_scatter,all_to_all")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -653,7 +841,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    if world > 1:
+    if args.sweep:
+        run_sweep_multi(args, rank, world, local_rank) if world > 1 else run_sweep_single(args)
+    elif world > 1:
         run_ours_multi(args, rank, world, local_rank)
     else:
         run_ours_single(args)
