@@ -1,8 +1,22 @@
 """dtorch_b200 -- B200-native thread-group collectives behind DTorch's DTensor redistribute.
 
-The C ABI (include/dtorch_b200.h, ``capi``) is the drop-in boundary: all-reduce (Partial->Replicate),
-all-gather (Shard->Replicate), reduce-scatter (Partial->Shard(0)) and all-to-all (Shard(i)->Shard(j)) as
-hand-written sm_100a kernels that move data through peer HBM over NVLink.
+* ``capi``: ctypes binding of the C ABI (include/dtorch_b200.h) -- all-reduce (Partial->Replicate), all-gather
+  (Shard->Replicate), reduce-scatter (Partial->Shard(0)) and all-to-all (Shard(i)->Shard(j)) as hand-written
+  sm_100a kernels that move data through peer HBM over NVLink.
+* ``DeviceMesh``, ``Shard``, ``Replicate``, ``Partial``, ``init_device_mesh``, ``DTensor`` (``redistribute``):
+  the reference's Python API over the C++ host layer (``_host``: ThreadGroup, kernel-stream threads,
+  redistribute executor).
 """
 
 __version__ = "0.1.0"
+
+_DTENSOR_NAMES = ("DeviceMesh", "Placement", "Shard", "Replicate", "Partial", "init_device_mesh", "DTensor",
+                  "cuda_device_of", "clear")
+
+
+def __getattr__(name):
+    if name in _DTENSOR_NAMES:
+        from . import dtensor
+
+        return getattr(dtensor, name)
+    raise AttributeError(name)

@@ -1,0 +1,241 @@
+"""DeviceMesh / Placement / DTensor.redistribute over the B200 collectives.
+
+The user-facing names and argument meaning follow the reference's Python API (python/dtorch/distributed_spec.py:
+``DeviceMesh``, ``Shard``, ``Replicate``, ``Partial``, ``init_device_mesh``; python/dtorch/tensor.py:299-351:
+``Tensor.redistribute``, ``redistribute_like``). A DTensor here is the set of its per-device local tensors;
+``redistribute`` runs the C++ executor (one kernel-stream thread per device, one ThreadGroup collective per
+changed mesh dim, ``dtorch_b200/csrc/host/redistribute.cpp``). ``from_torch`` / ``to_torch`` place and collect
+a whole tensor the way the reference's DistributedScather / DistributeGather do
+(dtorch/core/kernel/kernel_implement/distributed_scather_and_gather.cc:24-145); they are host-side helpers,
+not part of the collective path.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from typing import Dict, List, Optional, Sequence, Union
+
+import torch
+
+from . import _host
+
+
+class Placement:
+    """Replicate ("R"), Partial ("P", pending SUM) or Shard(dim) ("S<dim>")."""
+
+    def __init__(self, placement: str):
+        self._s = placement
+        if placement in ("R", "P"):
+            self._dim = None
+        elif placement.startswith("S"):
+            self._dim = int(placement[1:])
+        else:
+            raise ValueError(f"bad placement {placement!r}")
+
+    def __eq__(self, other) -> bool:
+        return isinstance(other, Placement) and other._s == self._s
+
+    def __hash__(self):
+        return hash(self._s)
+
+    def __repr__(self) -> str:
+        return self._s
+
+    def is_replicate(self) -> bool:
+        return self._s == "R"
+
+    def is_partial(self) -> bool:
+        return self._s == "P"
+
+    def is_shard(self) -> bool:
+        return self._dim is not None
+
+    def get_shard_index(self) -> int:
+        return self._dim
+
+
+def Shard(dim: int) -> Placement:  # noqa: N802 (reference API name)
+    return Placement(f"S{dim}")
+
+
+def Replicate() -> Placement:  # noqa: N802
+    return Placement("R")
+
+
+def Partial() -> Placement:  # noqa: N802
+    return Placement("P")
+
+
+class DeviceMesh:
+    """Global device ids arranged in a mesh. Only "cuda" meshes are served by this library; the reference's
+    CPU mesh is its own thread-group path (the test oracle), not a fallback."""
+
+    def __init__(self, device_type: str, mesh, mesh_dim_names: Optional[Sequence[str]] = None):
+        if device_type not in ("cuda", "gpu"):
+            raise ValueError("dtorch_b200 serves cuda device meshes only")
+        t = mesh if isinstance(mesh, torch.Tensor) else torch.tensor(mesh)
+        t = t.cpu().to(torch.int64)
+        if t.dim() == 0:
+            t = t.reshape(1)
+        self.mesh = t
+        self.device_type = "cuda"
+        self.dim_names = list(mesh_dim_names) if mesh_dim_names else []
+
+    @property
+    def shape(self):
+        return tuple(self.mesh.shape)
+
+    @property
+    def ndim(self) -> int:
+        return self.mesh.dim()
+
+    @property
+    def ids(self) -> List[int]:
+        return self.mesh.reshape(-1).tolist()
+
+    @property
+    def is_distributed(self) -> bool:
+        return self.mesh.numel() > 1
+
+    def __eq__(self, other) -> bool:
+        return isinstance(other, DeviceMesh) and torch.equal(self.mesh, other.mesh)
+
+    def __repr__(self) -> str:
+        return f"DeviceMesh('cuda', shape: {self.shape}, data: {self.mesh.tolist()})"
+
+
+def init_device_mesh(device_type: str, mesh_shape: Union[int, Sequence[int]],
+                     mesh_dim_names: Optional[Sequence[str]] = None) -> DeviceMesh:
+    """Mesh of devices 0..prod(shape)-1 in row-major order (python/dtorch/distributed_spec.py:179-194)."""
+    if isinstance(mesh_shape, int):
+        mesh_shape = (mesh_shape,)
+    mesh_shape = [s for s in mesh_shape if s is not None] or [1]
+    return DeviceMesh(device_type, torch.arange(math.prod(mesh_shape)).view(mesh_shape), mesh_dim_names)
+
+
+def cuda_device_of(global_id: int) -> int:
+    """CUDA ordinal of a global device id (all on device 0 when DTORCH_DTENSOR_IN_SAME_DEVICE=1)."""
+    return 0 if os.environ.get("DTORCH_DTENSOR_IN_SAME_DEVICE") == "1" else int(global_id)
+
+
+def _strings(placements: Sequence[Placement]) -> List[str]:
+    return [repr(p) for p in placements]
+
+
+def _merge_same_shard_dims(mesh: torch.Tensor, placements: List[Placement]):
+    """Merge mesh dims sharding the same tensor dim into one (DistributedSpec::MergeSameShardDim,
+    distributed_spec.cc:442-489), so a tensor dim sharded over several mesh dims splits row-major."""
+    groups: Dict[int, List[int]] = {}
+    for i, p in enumerate(placements):
+        if p.is_shard():
+            groups.setdefault(p.get_shard_index(), []).append(i)
+    merge = {g[0]: g for g in groups.values() if len(g) > 1}
+    if not merge:
+        return mesh, placements
+    perm, new_shape, new_p, used = [], [], [], set()
+    for i in range(mesh.dim()):
+        if i in used:
+            continue
+        dims = merge.get(i, [i])
+        for d in dims:
+            perm.append(d)
+            used.add(d)
+        new_shape.append(math.prod(mesh.shape[d] for d in dims))
+        new_p.append(placements[i])
+    return mesh.permute(perm).reshape(new_shape), new_p
+
+
+class DTensor:
+    """A distributed tensor: one local tensor per global device id of `device_mesh`."""
+
+    def __init__(self, locals_: Dict[int, torch.Tensor], device_mesh: DeviceMesh, placements: Sequence[Placement],
+                 shape: Sequence[int]):
+        self._locals = dict(locals_)
+        self.device_mesh = device_mesh
+        self.placements = list(placements)
+        self.shape = tuple(int(s) for s in shape)
+
+    @property
+    def dtype(self):
+        return next(iter(self._locals.values())).dtype
+
+    def local(self, device_id: int) -> torch.Tensor:
+        return self._locals[device_id]
+
+    @property
+    def locals(self) -> Dict[int, torch.Tensor]:
+        return dict(self._locals)
+
+    # -- placement of a whole tensor (host helpers) -------------------------------------------------------
+    @staticmethod
+    def from_torch(tensor: torch.Tensor, device_mesh: DeviceMesh, placements: Sequence[Placement]) -> "DTensor":
+        placements = _host.normalize(_strings(placements), list(device_mesh.shape), device_mesh.ids, tensor.dim())
+        placements = [Placement(p) for p in placements]
+        _host.check_valid(list(tensor.shape), list(device_mesh.shape), device_mesh.ids, _strings(placements))
+        mesh, plc = _merge_same_shard_dims(device_mesh.mesh, placements)
+        out: Dict[int, torch.Tensor] = {}
+
+        def scatter(t: torch.Tensor, m: torch.Tensor, i: int):
+            if i == len(plc):
+                gid = int(m.reshape(-1)[0])
+                out[gid] = t.contiguous().to(f"cuda:{cuda_device_of(gid)}")
+                return
+            n = m.shape[0]
+            p = plc[i]
+            if p.is_replicate():
+                parts = [t] * n
+            elif p.is_shard():
+                d = p.get_shard_index()
+                parts = list(torch.split(t, _host.shard_sizes(t.shape[d], n), d))
+            else:  # Partial: the tensor on the first, zeros elsewhere (distributed_scather_and_gather.cc:83-84)
+                parts = [t] + [torch.zeros_like(t)] * (n - 1)
+            for k in range(n):
+                scatter(parts[k], m[k], i + 1)
+
+        scatter(tensor, mesh, 0)
+        return DTensor(out, device_mesh, placements, tensor.shape)
+
+    def to_torch(self, device: Union[str, torch.device] = "cpu") -> torch.Tensor:
+        mesh, plc = _merge_same_shard_dims(self.device_mesh.mesh, self.placements)
+
+        def gather(m: torch.Tensor, i: int) -> torch.Tensor:
+            if i == len(plc):
+                return self._locals[int(m.reshape(-1)[0])].to(device)
+            p = plc[i]
+            if p.is_replicate():
+                return gather(m[0], i + 1)
+            parts = [gather(m[k], i + 1) for k in range(m.shape[0])]
+            if p.is_shard():
+                return torch.cat(parts, p.get_shard_index())
+            acc = parts[0]
+            for x in parts[1:]:
+                acc = acc + x
+            return acc
+
+        return gather(mesh, 0)
+
+    # -- redistribute (the hot path) -----------------------------------------------------------------------
+    def redistribute(self, device_mesh: Optional[DeviceMesh] = None,
+                     placements: Optional[Sequence[Placement]] = None) -> "DTensor":
+        """Tensor.redistribute (python/dtorch/tensor.py:299-309): same mesh, new placements."""
+        assert device_mesh is not None or placements is not None
+        device_mesh = device_mesh if device_mesh is not None else self.device_mesh
+        if device_mesh != self.device_mesh:
+            raise NotImplementedError("moving a DTensor between device meshes is not part of this library yet")
+        placements = list(placements) if placements is not None else list(self.placements)
+        new = _host.redistribute(self._locals, list(device_mesh.shape), device_mesh.ids, _strings(self.placements),
+                                 _strings(placements), list(self.shape))
+        normalized = _host.normalize(_strings(placements), list(device_mesh.shape), device_mesh.ids, len(self.shape))
+        return DTensor(new, device_mesh, [Placement(p) for p in normalized], self.shape)
+
+    def redistribute_like(self, other: "DTensor") -> "DTensor":
+        return self.redistribute(device_mesh=other.device_mesh, placements=other.placements)
+
+    def __repr__(self) -> str:
+        return f"DTensor(shape={self.shape}, mesh={self.device_mesh}, placements={self.placements})"
+
+
+def clear() -> None:
+    """Destroy the kernel-stream threads and communicators (e.g. before switching device-mapping modes)."""
+    _host.clear()

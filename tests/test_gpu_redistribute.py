@@ -1,0 +1,176 @@
+"""GPU: the reference-facing host layer -- ThreadGroup (the reference's communicator API) and
+DTensor.redistribute -- on the B200 collectives, on the cases of the reference's own tests:
+
+* dtorch/tests/test_nccl.cc:27-45: one thread per rank, ThreadGroup.AllReduce of ones == group size.
+* python/dtorch/test/test_distributed_tensor.py:146-393: 1-D mesh [0, 1] with even (4, 8) and uneven (5, 9)
+  shapes (P->R, P->S0, S0->R, S1->R, S1->S0, S0->S1, R->S1), 2-D mesh (4, 2), 3-D mesh (2, 2, 2).
+
+Each runs in the reference's two modes: same-device emulation (DTORCH_DTENSOR_IN_SAME_DEVICE=1: every rank
+on cuda:0, one kernel per collective) and peer mode (rank r on cuda:r) when enough GPUs are present. Results
+are compared with the whole tensor (as the reference does, allclose rtol 1e-5 / atol 1e-8 -- here
+bit-exact, since moves are copies and the fp32 sums fold in the reference's order), and sums with the
+oracle fold.
+"""
+
+import os
+import threading
+
+import numpy as np
+import pytest
+import torch
+
+import dtorch_b200 as dtb
+from oracle.oracle import Restatement
+
+pytestmark = pytest.mark.gpu
+R = Restatement()
+
+
+def ngpu():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.fixture(params=["same", "peer"])
+def mode(request):
+    if ngpu() < 1:
+        pytest.skip("no CUDA device")
+    old = os.environ.get("DTORCH_DTENSOR_IN_SAME_DEVICE")
+    if request.param == "same":
+        os.environ["DTORCH_DTENSOR_IN_SAME_DEVICE"] = "1"
+    else:
+        os.environ.pop("DTORCH_DTENSOR_IN_SAME_DEVICE", None)
+    os.environ.setdefault("DTORCH_COMM_TIMEOUT_SECOND", "30")
+    dtb.clear()
+    yield request.param
+    dtb.clear()
+    if old is None:
+        os.environ.pop("DTORCH_DTENSOR_IN_SAME_DEVICE", None)
+    else:
+        os.environ["DTORCH_DTENSOR_IN_SAME_DEVICE"] = old
+
+
+def need(mode, n):
+    if mode == "peer" and ngpu() < n:
+        pytest.skip(f"peer mode on {n} devices needs {n} GPUs")
+
+
+def test_thread_group_all_reduce_of_ones(mode):
+    n = 2 if mode == "same" or ngpu() < 8 else 8
+    need(mode, n)
+    ids = list(range(n))
+    results = [None] * n
+    errors = []
+
+    def rank_fn(r):
+        try:
+            dev = dtb.cuda_device_of(r)
+            with torch.cuda.device(dev):
+                tg = dtb.dtensor._host.get_thread_group(ids, r)
+                assert tg.get_rank() == r and tg.get_world_size() == n and tg.get_global_device_id() == r
+                x = torch.ones(1000, 1000, device=f"cuda:{dev}")
+                tg.barrier()
+                y = tg.all_reduce(x)
+                tg.barrier()
+                torch.cuda.current_stream(dev).synchronize()
+                results[r] = y
+        except BaseException as e:  # noqa: BLE001
+            errors.append(e)
+
+    th = [threading.Thread(target=rank_fn, args=(r,)) for r in range(n)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(60)
+    assert not errors, errors
+    for y in results:
+        assert torch.equal(y.cpu(), torch.full((1000, 1000), float(n)))
+
+
+def check_redistribute(mesh, full, src, dst, expected=None):
+    x = dtb.DTensor.from_torch(full, mesh, src)
+    y = x.redistribute(device_mesh=mesh, placements=dst)
+    torch.cuda.synchronize()
+    got = y.to_torch()
+    want = full if expected is None else expected
+    assert got.shape == want.shape
+    assert torch.equal(got, want), f"{src} -> {dst}"
+    return y
+
+
+@pytest.mark.parametrize("shape", [(4, 8), (5, 9)])
+def test_redistribute_1d_like_reference(mode, shape):
+    need(mode, 2)
+    g = torch.Generator().manual_seed(0)
+    full = torch.rand(*shape, generator=g)
+    mesh = dtb.DeviceMesh("cuda", [0, 1])
+    S, Rp, P = dtb.Shard, dtb.Replicate, dtb.Partial
+    # Partial built as the reference builds it: the tensor on rank 0, zeros elsewhere
+    check_redistribute(mesh, full, [P()], [Rp()])
+    if shape[0] % 2 == 0:
+        y = check_redistribute(mesh, full, [P()], [S(0)])
+        assert y.local(0).shape == (shape[0] // 2, shape[1])
+    check_redistribute(mesh, full, [S(0)], [Rp()])
+    check_redistribute(mesh, full, [S(-1)], [Rp()])
+    check_redistribute(mesh, full, [S(-1)], [S(0)])
+    check_redistribute(mesh, full, [S(0)], [S(1)])
+    check_redistribute(mesh, full, [Rp()], [S(1)])
+    # local shapes follow the shard rule
+    y = dtb.DTensor.from_torch(full, mesh, [S(1)])
+    assert y.local(0).shape[1] == (shape[1] + 1) // 2 and y.local(1).shape[1] == shape[1] // 2
+
+
+def test_redistribute_partial_sum_matches_oracle(mode):
+    need(mode, 4)
+    n = 4
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(1)
+    parts = [torch.randn(64, 33, generator=g) for _ in range(n)]
+    locals_ = {r: parts[r].to(f"cuda:{dtb.cuda_device_of(r)}") for r in range(n)}
+    x = dtb.DTensor(locals_, mesh, [dtb.Partial()], (64, 33))
+    want = R.fold_sum([p.numpy() for p in parts], 0, storage_round=True)
+    y = x.redistribute(placements=[dtb.Replicate()])
+    torch.cuda.synchronize()
+    for r in range(n):
+        assert np.array_equal(y.local(r).cpu().numpy(), want)
+    z = x.redistribute(placements=[dtb.Shard(0)])
+    torch.cuda.synchronize()
+    assert np.array_equal(z.to_torch().numpy(), want)
+
+
+def test_redistribute_2d_like_reference(mode):
+    need(mode, 8)
+    mesh = dtb.init_device_mesh("cuda", (4, 2))
+    g = torch.Generator().manual_seed(2)
+    full = torch.rand(4, 16, generator=g)
+    S, Rp = dtb.Shard, dtb.Replicate
+    check_redistribute(mesh, full, [S(0), S(1)], [Rp(), S(1)])
+    check_redistribute(mesh, full, [S(0), S(1)], [S(0), Rp()])
+    check_redistribute(mesh, full, [Rp(), Rp()], [S(1), Rp()])
+    check_redistribute(mesh, full, [Rp(), Rp()], [S(1), S(1)])
+    check_redistribute(mesh, full, [S(0), S(1)], [Rp(), Rp()])
+
+
+def test_redistribute_3d_like_reference(mode):
+    need(mode, 8)
+    mesh = dtb.init_device_mesh("cuda", (2, 2, 2))
+    g = torch.Generator().manual_seed(3)
+    full = torch.rand(2, 16, 128, 128, generator=g)
+    S, Rp = dtb.Shard, dtb.Replicate
+    check_redistribute(mesh, full, [S(0), S(2), S(2)], [Rp(), Rp(), Rp()])
+    check_redistribute(mesh, full, [Rp(), Rp(), Rp()], [S(0), S(2), S(2)])
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_ulysses_swap_and_back(mode, n):
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(n)
+    full = torch.randn(1, 96, 12, 16, generator=g).to(torch.bfloat16)  # (B, S, H, D); uneven heads at n=8
+    x = dtb.DTensor.from_torch(full, mesh, [dtb.Shard(1)])
+    y = x.redistribute(placements=[dtb.Shard(2)])  # sequence-sharded -> head-sharded
+    z = y.redistribute(placements=[dtb.Shard(1)])  # and back
+    torch.cuda.synchronize()
+    assert torch.equal(y.to_torch(), full)
+    assert torch.equal(z.to_torch(), full)
+    for r in range(n):
+        assert torch.equal(z.local(r).cpu(), x.local(r).cpu())

@@ -1,0 +1,64 @@
+"""CPU: the placement algebra of the host layer (dtorch_b200/csrc/host/placement.cpp) against the reference's
+rules, on cases worked out from dtorch/api/cpp/distributed_spec.cc and thread_group_manager.cc."""
+
+import pytest
+
+h = pytest.importorskip("dtorch_b200._host")
+
+
+def test_shard_sizes():
+    assert h.shard_sizes(9, 2) == [5, 4]
+    assert h.shard_sizes(17, 8) == [3, 2, 2, 2, 2, 2, 2, 2]
+    assert h.shard_sizes(65536, 8) == [8192] * 8
+
+
+def test_convert_order_shard_to_replicate_last_back_to_front():
+    # distributed_spec.cc:327-343: changed dims in order, then S->R dims reversed
+    assert h.get_convert_order(["S0", "S1", "P"], ["R", "R", "R"]) == [2, 1, 0]
+    assert h.get_convert_order(["S0", "R"], ["R", "S1"]) == [1, 0]
+    assert h.get_convert_order(["S0", "S2", "S2"], ["R", "R", "R"]) == [2, 1, 0]
+    assert h.get_convert_order(["R", "R"], ["S1", "S1"]) == [0, 1]
+    assert h.get_convert_order(["R"], ["R"]) == []
+    assert h.get_diff_dims(["S0", "S1"], ["R", "S1"]) == [0]
+
+
+def test_normalize():
+    assert h.normalize(["S-1"], [2], [0, 1], 2) == ["S1"]
+    assert h.normalize(["S0", "S1", "P"], [2, 1, 4], list(range(8)), 3) == ["S0", "R", "P"]
+
+
+def test_group_device_ids():
+    ids = list(range(8))
+    assert h.group_device_ids([4, 2], ids, 0, 3) == [1, 3, 5, 7]
+    assert h.group_device_ids([4, 2], ids, 1, 3) == [2, 3]
+    assert h.group_device_ids([2, 2, 2], ids, 1, 5) == [5, 7]
+    assert h.group_device_ids([8], ids, 0, 6) == ids
+    assert h.group_device_ids([2, 2], [7, 5, 3, 1], 0, 1) == [5, 1]
+
+
+def test_compute_local_shapes():
+    assert h.compute_local_shapes([5, 9], [2], [0, 1], ["S1"]) == {0: [5, 5], 1: [5, 4]}
+    assert h.compute_local_shapes([4, 8], [2], [0, 1], ["S0"]) == {0: [2, 8], 1: [2, 8]}
+    even = h.compute_local_shapes([4, 16], [4, 2], list(range(8)), ["S0", "S1"])
+    assert all(v == [1, 8] for v in even.values())
+    # one tensor dim sharded by two mesh dims: row-major over them, uneven sizes by the shard rule
+    merged = h.compute_local_shapes([4, 17], [4, 2], list(range(8)), ["S1", "S1"])
+    assert merged == {0: [4, 3], **{i: [4, 2] for i in range(1, 8)}}
+    p = h.compute_local_shapes([6, 5], [2], [0, 1], ["P"])
+    assert p == {0: [6, 5], 1: [6, 5]}
+
+
+@pytest.mark.parametrize("shape,mesh,ids,pl", [
+    ([4, 8], [2], [0, 1], ["S2"]),      # shard dim beyond the rank
+    ([1, 8], [2], [0, 1], ["S0"]),      # fewer rows than shards
+    ([4, 8], [2], [0, 0], ["S0"]),      # duplicate device ids
+    ([4, 8], [2], [0, 1], ["S0", "R"]),  # placements longer than the mesh
+])
+def test_check_valid_rejects(shape, mesh, ids, pl):
+    with pytest.raises(Exception):
+        h.check_valid(shape, mesh, ids, pl)
+
+
+def test_check_valid_accepts():
+    h.check_valid([5, 9], [2], [0, 1], ["S1"])
+    h.check_valid([2, 16, 128, 128], [2, 2, 2], list(range(8)), ["S0", "S2", "S2"])
