@@ -481,6 +481,55 @@ def heap_tensor(base, offset, numel, dtype, device):
     return t.view(dtype) if dtype != torch.float32 else t
 
 
+def share_fd(rank, n, fd, tag):
+    """Hand rank 0's file descriptor to every other rank (SCM_RIGHTS over a Unix socket)."""
+    import socket
+
+    import torch.distributed as dist
+
+    path = f"/tmp/dtb_{os.getuid()}_{os.environ.get('MASTER_PORT', '0')}_{tag}.sock"
+    if rank == 0:
+        if os.path.exists(path):
+            os.unlink(path)
+        srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        srv.bind(path)
+        srv.listen(n)
+        dist.barrier()
+        for _ in range(n - 1):
+            conn, _ = srv.accept()
+            socket.send_fds(conn, [b"f"], [fd])
+            conn.close()
+        srv.close()
+        os.unlink(path)
+        dist.barrier()
+        return fd
+    dist.barrier()
+    c = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    c.connect(path)
+    _, fds, _, _ = socket.recv_fds(c, 16, 1)
+    c.close()
+    dist.barrier()
+    return fds[0]
+
+
+def setup_nvls(comm, rank, n, nbytes):
+    """Bind an NVLS buffer of `nbytes` on every rank of a multi-process communicator; False if unsupported."""
+    import torch.distributed as dist
+
+    ok = torch.tensor([1 if comm.nvls_supported() else 0], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok.item()) == 0:
+        return False
+    fd = comm.nvls_create(nbytes) if rank == 0 else -1
+    fd = share_fd(rank, n, fd, "nvls")
+    comm.nvls_attach(fd, nbytes)
+    dist.barrier()  # every device added before any rank binds memory
+    comm.nvls_bind()
+    dist.barrier()
+    os.close(fd)
+    return True
+
+
 def run_ours_multi(args, rank, world, local_rank):
     """One rank per process; peers IPC-mapped through the communicator's symmetric heap."""
     import datetime
@@ -540,11 +589,25 @@ def run_ours_multi(args, rank, world, local_rank):
         del full
     stream = torch.cuda.current_stream(dev)
     code = capi.dtype_code(dtype) if dtype in (torch.float32, torch.bfloat16, torch.float16) else 0
+    # all-reduce: the two-shot P2P kernel (rank-order fold) on the heap buffers, and -- where the switch
+    # supports it and it is faster (n >= 4) -- the NVLS kernel on buffers bound to a multicast object
+    algo = "p2p two-shot (rank-order fp32 fold)"
+    ar_flags = 0
+    xp, yp = x, y
+    if op == "all_reduce" and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
+        if setup_nvls(comm, rank, n, 2 * in_bytes):
+            nb, _ = comm.nvls_buffer(rank)
+            xn = heap_tensor(nb, 0, in_numel, dtype, dev)
+            yn = heap_tensor(nb, in_bytes, out_numel, dtype, dev)
+            xn.copy_(x)
+            x, y = xn, yn
+            algo = "nvls (in-switch reduction, fp32 accumulate)"
+            ar_flags = capi.DT_ALGO_NVLS
 
     def step():
         s = stream.cuda_stream
         if op == "all_reduce":
-            comm.all_reduce(rank, x.data_ptr(), y.data_ptr(), in_numel, code, 0, s)
+            comm.all_reduce(rank, x.data_ptr(), y.data_ptr(), in_numel, code, ar_flags, s)
         elif op == "reduce_scatter":
             comm.reduce_scatter(rank, x.data_ptr(), y.data_ptr(), out_numel, code, 0, s)
         elif op == "all_gather":
@@ -567,6 +630,19 @@ def run_ours_multi(args, rank, world, local_rank):
     dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms = float(t_max.item())
     err = comm.error(rank)
+    p2p_bus = None
+    if xp is not x:  # the rank-order P2P kernel on the same message, for comparison
+        def pstep():
+            comm.all_reduce(rank, xp.data_ptr(), yp.data_ptr(), in_numel, code, capi.DT_ALGO_TWOSHOT, stream.cuda_stream)
+
+        for _ in range(3):
+            pstep()
+        torch.cuda.synchronize()
+        dist.barrier()
+        pms = time_steps(pstep, args.steps, stream)
+        t_max = torch.tensor([pms], device=dev)
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        p2p_bus = msg * bus_factor(op, n) / (float(t_max.item()) / 1e3) / 1e9
     # end to end: pinned host input -> heap, collective, heap output -> pinned host
     h_in = x.cpu().pin_memory()
     h_out = torch.empty(out_numel, dtype=dtype).pin_memory()
@@ -629,6 +705,8 @@ def run_ours_multi(args, rank, world, local_rank):
             "bus_gbs_per_rank": round(bus, 2),
             "pct_nvlink_peak": round(bus / NVLINK_NOMINAL_GBS, 4),
             "nccl_bus_gbs_per_rank": None if nccl_bus is None else round(nccl_bus, 2),
+            "algorithm": algo,
+            "p2p_bus_gbs_per_rank": None if p2p_bus is None else round(p2p_bus, 2),
             "roofline": {"bound": "nvlink", "achieved": round(bus, 1), "peak": NVLINK_PEER_COPY_GBS, "unit": "GB/s",
                          "frac": round(bus / NVLINK_PEER_COPY_GBS, 4), "traffic": None,
                          "peak_source": "measured peer copy per direction (pool reference); nominal 900"},
@@ -679,6 +757,10 @@ def run_sweep_multi(args, rank, world, local_rank):
     base, _ = comm.heap(rank)
     stream = torch.cuda.current_stream(dev)
     ops = args.sweep_ops.split(",")
+    nvls_base = 0
+    if "all_reduce" in ops and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
+        if setup_nvls(comm, rank, n, 2 * max_bytes + (4 << 20)):
+            nvls_base, _ = comm.nvls_buffer(rank)
     for op in ops:
         for dtype in ([torch.bfloat16, torch.float32] if op in ("all_reduce", "reduce_scatter") else [torch.bfloat16]):
             es = torch.tensor([], dtype=dtype).element_size()
@@ -727,8 +809,19 @@ def run_sweep_multi(args, rank, world, local_rank):
                     else:
                         dist.all_to_all_single(ya, xa)
 
+                impls = [("ours", ours), ("nccl", nccl)]
+                if op == "all_reduce" and nvls_base and (in_n * es) % 16 == 0:
+                    xn = heap_tensor(nvls_base, 0, in_n, dtype, dev)
+                    yn = heap_tensor(nvls_base, max_bytes + (2 << 20), out_n, dtype, dev)
+                    xn.copy_(x)
+
+                    def ours_nvls():
+                        comm.all_reduce(rank, xn.data_ptr(), yn.data_ptr(), in_n, code, capi.DT_ALGO_NVLS,
+                                        stream.cuda_stream)
+
+                    impls.append(("nvls", ours_nvls))
                 res = {}
-                for name, fn in (("ours", ours), ("nccl", nccl)):
+                for name, fn in impls:
                     for _ in range(3):
                         fn()
                     torch.cuda.synchronize()
@@ -749,11 +842,15 @@ def run_sweep_multi(args, rank, world, local_rank):
                 busf = bus_factor(op, n)
                 msg = in_n * es if op != "all_gather" else out_n * es
                 if rank == 0:
-                    print(json.dumps({"sweep": op, "n_gpus": n, "dtype": DT_NAME[dtype], "bytes": msg,
-                                      "ours_ms": round(res["ours"], 5), "nccl_ms": round(res["nccl"], 5),
-                                      "ours_bus_gbs": round(msg * busf / res["ours"] / 1e6, 2),
-                                      "nccl_bus_gbs": round(msg * busf / res["nccl"] / 1e6, 2),
-                                      "device_error": comm.error(rank)}), flush=True)
+                    line = {"sweep": op, "n_gpus": n, "dtype": DT_NAME[dtype], "bytes": msg,
+                            "ours_ms": round(res["ours"], 5), "nccl_ms": round(res["nccl"], 5),
+                            "ours_bus_gbs": round(msg * busf / res["ours"] / 1e6, 2),
+                            "nccl_bus_gbs": round(msg * busf / res["nccl"] / 1e6, 2),
+                            "device_error": comm.error(rank)}
+                    if "nvls" in res:
+                        line["nvls_ms"] = round(res["nvls"], 5)
+                        line["nvls_bus_gbs"] = round(msg * busf / res["nvls"] / 1e6, 2)
+                    print(json.dumps(line), flush=True)
                 del xa, ya
     dist.barrier()
     comm.destroy()
@@ -903,6 +1000,8 @@ def main():
     p.add_argument("--op", choices=list(CONFIGS), default="all_reduce")
     p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     p.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end leg (profiling runs)")
+    p.add_argument("--algo", choices=["auto", "p2p", "nvls"], default="auto",
+                   help="all-reduce algorithm at N > 1: auto = NVLS where supported and n >= 4, else P2P two-shot")
     p.add_argument("--sweep", action="store_true", help="C5 message-size sweep, one JSON line per point")
     p.add_argument("--link-probe", action="store_true", help="per-direction NVLink throughput of each transfer "
                    "mechanism between GPU 0 and GPU 1 (diagnostic, one JSON line per point)")

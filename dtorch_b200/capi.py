@@ -28,6 +28,7 @@ DT_ACCUM_FP32 = 0x0
 DT_ACCUM_STORAGE = 0x1
 DT_ALGO_ONESHOT = 0x10
 DT_ALGO_TWOSHOT = 0x20
+DT_ALGO_NVLS = 0x40
 
 MAX_RANKS = 8
 
@@ -63,6 +64,12 @@ SIGNATURES = [
     ("dt_local_all_gather", _I, [_I, _P, _P, _SZ, _P, _SZ, _P]),
     ("dt_local_all_to_all", _I, [_I, _P, _P, _I, _P, _I, _I, _P, _SZ, _P]),
     ("dt_kernel_launch_count", ctypes.c_uint64, []),
+    ("dt_comm_nvls_supported", _I, [_P, _P]),
+    ("dt_comm_nvls_alloc", _I, [_P, _SZ]),
+    ("dt_comm_nvls_create", _I, [_P, _SZ, _P]),
+    ("dt_comm_nvls_attach", _I, [_P, _I, _SZ]),
+    ("dt_comm_nvls_bind", _I, [_P]),
+    ("dt_comm_nvls_buffer", _I, [_P, _I, _P, _P]),
 ]
 
 
@@ -172,6 +179,32 @@ class Comm:
         base = ctypes.c_void_p()
         size = ctypes.c_size_t()
         check(lib().dt_comm_heap(self._h, rank, ctypes.byref(base), ctypes.byref(size)), "dt_comm_heap")
+        return base.value or 0, size.value
+
+    # ---- NVLS buffer ----
+    def nvls_supported(self) -> bool:
+        v = ctypes.c_int()
+        check(lib().dt_comm_nvls_supported(self._h, ctypes.byref(v)), "dt_comm_nvls_supported")
+        return bool(v.value)
+
+    def nvls_alloc(self, nbytes: int) -> None:
+        check(lib().dt_comm_nvls_alloc(self._h, nbytes), "dt_comm_nvls_alloc")
+
+    def nvls_create(self, nbytes: int) -> int:
+        fd = ctypes.c_int(-1)
+        check(lib().dt_comm_nvls_create(self._h, nbytes, ctypes.byref(fd)), "dt_comm_nvls_create")
+        return fd.value
+
+    def nvls_attach(self, fd: int, nbytes: int) -> None:
+        check(lib().dt_comm_nvls_attach(self._h, fd, nbytes), "dt_comm_nvls_attach")
+
+    def nvls_bind(self) -> None:
+        check(lib().dt_comm_nvls_bind(self._h), "dt_comm_nvls_bind")
+
+    def nvls_buffer(self, rank: int):
+        base = ctypes.c_void_p()
+        size = ctypes.c_size_t()
+        check(lib().dt_comm_nvls_buffer(self._h, rank, ctypes.byref(base), ctypes.byref(size)), "dt_comm_nvls_buffer")
         return base.value or 0, size.value
 
     def set_timeout_ms(self, ms: int) -> None:

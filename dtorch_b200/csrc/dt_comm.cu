@@ -21,6 +21,9 @@
 #include <unordered_map>
 #include <vector>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "../../include/dtorch_b200.h"
 #include "dt_kernels.cuh"
 
@@ -96,6 +99,11 @@ struct RankState {
     uint32_t* peer_flags[kMaxRanks] = {};  // flags of rank r as addressed from this rank's device
     char* peer_heap[kMaxRanks] = {};       // heap of rank r as addressed from this rank's device
     bool imported[kMaxRanks] = {};         // peer slab opened through IPC (must be closed)
+    // NVLS buffer: this rank's memory bound to the communicator's multicast object
+    char* nvls_uc = nullptr;                     // unicast mapping (this rank's copy)
+    char* nvls_mc = nullptr;                     // multicast mapping (every rank's copy at once)
+    CUmemGenericAllocationHandle nvls_phys = 0;  // physical memory bound to the multicast object
+    bool nvls_bound = false;
 };
 
 // What one rank publishes at a rendezvous.
@@ -125,6 +133,11 @@ struct dt_comm {
     cudaEvent_t done = nullptr;
     std::atomic<uint64_t> launched_gen{0};
     std::atomic<int> launch_status{0};
+    // NVLS (NVLink multicast) buffer
+    CUmemGenericAllocationHandle nvls_mc_handle = 0;
+    bool nvls_have_mc = false;
+    size_t nvls_size = 0;
+    CUdeviceptr nvls_mc_va = 0;  // single process: one multicast mapping shared by every rank
 };
 
 namespace {
@@ -578,6 +591,191 @@ int same_device_call(dt_comm* c, int rank, const void* in, void* out, cudaStream
     return DT_OK;
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// CUDA driver entry points for NVLink multicast (looked up at run time through the runtime, so the library
+// has no link-time dependency on libcuda)
+// ---------------------------------------------------------------------------------------------------------
+struct Driver {
+    PFN_cuDeviceGet deviceGet = nullptr;
+    PFN_cuDeviceGetAttribute deviceGetAttribute = nullptr;
+    PFN_cuMulticastCreate mcCreate = nullptr;
+    PFN_cuMulticastAddDevice mcAddDevice = nullptr;
+    PFN_cuMulticastBindMem mcBindMem = nullptr;
+    PFN_cuMulticastUnbind mcUnbind = nullptr;
+    PFN_cuMulticastGetGranularity mcGranularity = nullptr;
+    PFN_cuMemCreate memCreate = nullptr;
+    PFN_cuMemRelease memRelease = nullptr;
+    PFN_cuMemAddressReserve addressReserve = nullptr;
+    PFN_cuMemAddressFree addressFree = nullptr;
+    PFN_cuMemMap memMap = nullptr;
+    PFN_cuMemUnmap memUnmap = nullptr;
+    PFN_cuMemSetAccess memSetAccess = nullptr;
+    PFN_cuMemGetAllocationGranularity allocGranularity = nullptr;
+    PFN_cuMemExportToShareableHandle exportHandle = nullptr;
+    PFN_cuMemImportFromShareableHandle importHandle = nullptr;
+    bool ok = false;
+    std::string missing;
+};
+
+const Driver& driver() {
+    static Driver d = [] {
+        Driver r;
+        auto get = [&r](const char* name, void** fn) {
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess ||
+                *fn == nullptr) {
+                cudaGetLastError();
+                if (r.missing.empty()) r.missing = name;
+                *fn = nullptr;
+            }
+        };
+        get("cuDeviceGet", reinterpret_cast<void**>(&r.deviceGet));
+        get("cuDeviceGetAttribute", reinterpret_cast<void**>(&r.deviceGetAttribute));
+        get("cuMulticastCreate", reinterpret_cast<void**>(&r.mcCreate));
+        get("cuMulticastAddDevice", reinterpret_cast<void**>(&r.mcAddDevice));
+        get("cuMulticastBindMem", reinterpret_cast<void**>(&r.mcBindMem));
+        get("cuMulticastUnbind", reinterpret_cast<void**>(&r.mcUnbind));
+        get("cuMulticastGetGranularity", reinterpret_cast<void**>(&r.mcGranularity));
+        get("cuMemCreate", reinterpret_cast<void**>(&r.memCreate));
+        get("cuMemRelease", reinterpret_cast<void**>(&r.memRelease));
+        get("cuMemAddressReserve", reinterpret_cast<void**>(&r.addressReserve));
+        get("cuMemAddressFree", reinterpret_cast<void**>(&r.addressFree));
+        get("cuMemMap", reinterpret_cast<void**>(&r.memMap));
+        get("cuMemUnmap", reinterpret_cast<void**>(&r.memUnmap));
+        get("cuMemSetAccess", reinterpret_cast<void**>(&r.memSetAccess));
+        get("cuMemGetAllocationGranularity", reinterpret_cast<void**>(&r.allocGranularity));
+        get("cuMemExportToShareableHandle", reinterpret_cast<void**>(&r.exportHandle));
+        get("cuMemImportFromShareableHandle", reinterpret_cast<void**>(&r.importHandle));
+        r.ok = r.missing.empty();
+        return r;
+    }();
+    return d;
+}
+
+#define DT_CU(call)                                                                                     \
+    do {                                                                                                \
+        CUresult r_ = (call);                                                                           \
+        if (r_ != CUDA_SUCCESS) return fail(DT_ERR_CUDA, std::string(#call) + ": CUresult " + std::to_string(r_)); \
+    } while (0)
+
+int nvls_device_supported(int dev, bool* yes) {
+    const Driver& D = driver();
+    if (!D.ok) return fail(DT_ERR_UNSUPPORTED, "CUDA driver entry point missing: " + D.missing);
+    CUdevice cu = 0;
+    DT_CU(D.deviceGet(&cu, dev));
+    int v = 0;
+    DT_CU(D.deviceGetAttribute(&v, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, cu));
+    *yes = v != 0;
+    return DT_OK;
+}
+
+// Multicast and allocation granularity of `dev` for `n` devices; the buffer size is a multiple of both.
+int nvls_granularity(int dev, int n, size_t* gran) {
+    const Driver& D = driver();
+    CUmulticastObjectProp mp{};
+    mp.numDevices = static_cast<unsigned int>(n);
+    mp.size = 1;
+    mp.handleTypes = 0;
+    size_t g_mc = 0, g_alloc = 0;
+    DT_CU(D.mcGranularity(&g_mc, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED));
+    CUmemAllocationProp ap{};
+    ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    ap.location.id = dev;
+    DT_CU(D.allocGranularity(&g_alloc, &ap, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED));
+    *gran = std::max(g_mc, g_alloc);
+    return DT_OK;
+}
+
+// Physical memory of `rank` on its device, bound to the multicast object, mapped at a unicast address that
+// the listed devices may access.
+int nvls_bind_rank(dt_comm* c, int rank, const int* access_devs, int n_access) {
+    const Driver& D = driver();
+    RankState& s = c->r[rank];
+    CUmemAllocationProp ap{};
+    ap.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    ap.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    ap.location.id = s.dev;
+    // memory bound to a multicast object requests the object's shareable handle type
+    if (c->multiprocess) ap.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+    DT_CU(D.memCreate(&s.nvls_phys, c->nvls_size, &ap, 0));
+    DT_CU(D.mcBindMem(c->nvls_mc_handle, 0, s.nvls_phys, 0, c->nvls_size, 0));
+    s.nvls_bound = true;
+    CUdeviceptr va = 0;
+    DT_CU(D.addressReserve(&va, c->nvls_size, 0, 0, 0));
+    DT_CU(D.memMap(va, c->nvls_size, 0, s.nvls_phys, 0));
+    s.nvls_uc = reinterpret_cast<char*>(va);
+    std::vector<CUmemAccessDesc> acc(static_cast<size_t>(n_access));
+    for (int i = 0; i < n_access; ++i) {
+        acc[i].location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+        acc[i].location.id = access_devs[i];
+        acc[i].flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+    }
+    DT_CU(D.memSetAccess(va, c->nvls_size, acc.data(), acc.size()));
+    return DT_OK;
+}
+
+// Multicast mapping accessible from the listed devices.
+int nvls_map_multicast(dt_comm* c, const int* access_devs, int n_access, CUdeviceptr* out) {
+    const Driver& D = driver();
+    CUdeviceptr va = 0;
+    DT_CU(D.addressReserve(&va, c->nvls_size, 0, 0, 0));
+    DT_CU(D.memMap(va, c->nvls_size, 0, c->nvls_mc_handle, 0));
+    std::vector<CUmemAccessDesc> acc(static_cast<size_t>(n_access));
+    for (int i = 0; i < n_access; ++i) {
+        acc[i].location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+        acc[i].location.id = access_devs[i];
+        acc[i].flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+    }
+    DT_CU(D.memSetAccess(va, c->nvls_size, acc.data(), acc.size()));
+    *out = va;
+    return DT_OK;
+}
+
+// Release every NVLS resource of the communicator (after its devices were synchronized).
+void nvls_release(dt_comm* c) {
+    if (!c->nvls_have_mc) return;
+    const Driver& D = driver();
+    for (int i = 0; i < kMaxRanks; ++i) {
+        RankState& s = c->r[i];
+        if (s.dev < 0) continue;
+        cudaSetDevice(s.dev);
+        if (s.nvls_mc != nullptr && c->nvls_mc_va == 0) {
+            D.memUnmap(reinterpret_cast<CUdeviceptr>(s.nvls_mc), c->nvls_size);
+            D.addressFree(reinterpret_cast<CUdeviceptr>(s.nvls_mc), c->nvls_size);
+        }
+        if (s.nvls_uc != nullptr) {
+            D.memUnmap(reinterpret_cast<CUdeviceptr>(s.nvls_uc), c->nvls_size);
+            D.addressFree(reinterpret_cast<CUdeviceptr>(s.nvls_uc), c->nvls_size);
+        }
+        if (s.nvls_bound) {
+            CUdevice cu = 0;
+            if (D.deviceGet(&cu, s.dev) == CUDA_SUCCESS) D.mcUnbind(c->nvls_mc_handle, cu, 0, c->nvls_size);
+        }
+        if (s.nvls_phys != 0) D.memRelease(s.nvls_phys);
+        s.nvls_uc = s.nvls_mc = nullptr;
+        s.nvls_phys = 0;
+        s.nvls_bound = false;
+    }
+    if (c->nvls_mc_va != 0) {
+        D.memUnmap(c->nvls_mc_va, c->nvls_size);
+        D.addressFree(c->nvls_mc_va, c->nvls_size);
+        c->nvls_mc_va = 0;
+    }
+    D.memRelease(c->nvls_mc_handle);
+    c->nvls_have_mc = false;
+    c->nvls_size = 0;
+}
+
+template <int DT>
+int launch_nvls_t(const NvlsArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want) {
+    auto k = k_allreduce_nvls<DT>;
+    int grid = 1;
+    pick_grid(k, dev, num_sms, want, kReduceBlocksPerSM, &grid);
+    k<<<grid, kThreads, 0, stream>>>(a);
+    return launch_check("k_allreduce_nvls");
+}
+
 int common_checks(dt_comm* c, int rank) {
     if (c == nullptr) return fail(DT_ERR_INVALID, "null communicator");
     if (!check_rank(c, rank)) return fail(DT_ERR_INVALID, "rank out of range for this communicator");
@@ -779,10 +977,15 @@ int dt_comm_destroy(dt_comm* c) {
     DeviceGuard device_guard;
     if (c == nullptr) return DT_OK;
     for (int i = 0; i < kMaxRanks; ++i) {
+        if (c->r[i].dev < 0) continue;
+        cudaSetDevice(c->r[i].dev);
+        cudaDeviceSynchronize();
+    }
+    nvls_release(c);
+    for (int i = 0; i < kMaxRanks; ++i) {
         RankState& s = c->r[i];
         if (s.dev < 0) continue;
         cudaSetDevice(s.dev);
-        cudaDeviceSynchronize();
         for (int j = 0; j < kMaxRanks; ++j)
             if (s.imported[j]) cudaIpcCloseMemHandle(s.peer_flags[j]);
         if (s.ready) cudaEventDestroy(s.ready);
@@ -856,6 +1059,49 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
     if (c->n == 1) {
         if (count > 0 && in != out) DT_CUDA(cudaMemcpyAsync(out, in, count * es, cudaMemcpyDeviceToDevice, stream));
         return DT_OK;
+    }
+    // NVLS: input and output inside the communicator's NVLS buffer (same offsets on every rank)
+    {
+        int64_t nv_in = -1, nv_out = -1;
+        const size_t bytes = count * es;
+        if (s.nvls_uc != nullptr && s.nvls_mc != nullptr && count > 0) {
+            const char* lo = s.nvls_uc;
+            const char* pi = static_cast<const char*>(in);
+            const char* po = static_cast<const char*>(out);
+            if (pi >= lo && pi + bytes <= lo + c->nvls_size && po >= lo && po + bytes <= lo + c->nvls_size) {
+                nv_in = pi - lo;
+                nv_out = po - lo;
+            }
+        }
+        const bool nvls_ok = nv_in >= 0 && nv_in % 16 == 0 && nv_out % 16 == 0 && bytes % 16 == 0;
+        const bool want_nvls = (flags & DT_ALGO_NVLS) != 0;
+        if (want_nvls && !nvls_ok)
+            return fail(DT_ERR_INVALID, "DT_ALGO_NVLS needs 16-byte aligned input and output inside the communicator's "
+                                        "NVLS buffer and a size that is a multiple of 16 bytes");
+        if (want_nvls && storage)
+            return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NVLS reduces in the switch with fp32 accumulation; "
+                                            "DT_ACCUM_STORAGE is not available with it");
+        const bool auto_nvls = (flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT | DT_ALGO_NVLS)) == 0 && nvls_ok && !storage &&
+                               c->n >= 4 && bytes >= (static_cast<size_t>(1) << 20);
+        if (want_nvls || auto_nvls) {
+            NvlsArgs na{};
+            const uint32_t epoch = ++s.epoch;
+            na.sig = make_sig(c, rank);
+            na.bar_start = 2 * epoch - 1;
+            na.bar_end = 2 * epoch;
+            na.mc_in = s.nvls_mc + nv_in;
+            na.mc_out = s.nvls_mc + nv_out;
+            const int64_t nvec = static_cast<int64_t>(bytes / 16);
+            na.vlo = nvec * rank / c->n;
+            na.vhi = nvec * (rank + 1) / c->n;
+            const int64_t per_rank = (nvec + c->n - 1) / c->n;
+            const int64_t want = std::max<int64_t>(1, (per_rank + kThreads * 4 - 1) / (kThreads * 4));
+            switch (dtype) {
+                case DT_FLOAT32: return launch_nvls_t<0>(na, s.dev, s.num_sms, stream, want);
+                case DT_BFLOAT16: return launch_nvls_t<1>(na, s.dev, s.num_sms, stream, want);
+                default: return launch_nvls_t<2>(na, s.dev, s.num_sms, stream, want);
+            }
+        }
     }
     ReduceArgs a{};
     const char* ins[kMaxRanks];
@@ -1131,6 +1377,151 @@ int dt_barrier(dt_comm* c, int rank, void* stream_v) {
     const uint32_t epoch = ++s.epoch;
     k_barrier<<<1, 32, 0, stream>>>(make_sig(c, rank), 2 * epoch - 1, 2 * epoch);
     return launch_check("k_barrier");
+}
+
+// ---- NVLS buffer ------------------------------------------------------------------------------------------
+
+int dt_comm_nvls_supported(dt_comm* c, int* supported) {
+    DeviceGuard device_guard;
+    if (c == nullptr || supported == nullptr) return fail(DT_ERR_INVALID, "null argument");
+    *supported = 0;
+    if (c->same_device || c->n < 2) return DT_OK;
+    for (int r = 0; r < c->n; ++r) {
+        if (c->multiprocess && r != c->local_rank) continue;
+        bool yes = false;
+        const int st = nvls_device_supported(c->r[r].dev, &yes);
+        if (st != DT_OK) return st == DT_ERR_UNSUPPORTED ? DT_OK : st;
+        if (!yes) return DT_OK;
+    }
+    *supported = 1;
+    return DT_OK;
+}
+
+int dt_comm_nvls_alloc(dt_comm* c, size_t bytes) {
+    DeviceGuard device_guard;
+    if (c == nullptr || bytes == 0) return fail(DT_ERR_INVALID, "null communicator or zero size");
+    if (c->multiprocess || c->same_device || c->n < 2)
+        return fail(DT_ERR_INVALID, "dt_comm_nvls_alloc needs a single-process peer communicator of >= 2 ranks");
+    if (c->nvls_have_mc) return fail(DT_ERR_STATE, "the communicator already has an NVLS buffer");
+    int supported = 0;
+    int st = dt_comm_nvls_supported(c, &supported);
+    if (st != DT_OK) return st;
+    if (!supported) return fail(DT_ERR_UNSUPPORTED, "NVLink multicast is not supported on these devices");
+    const Driver& D = driver();
+    size_t gran = 0;
+    DT_CUDA(cudaSetDevice(c->r[0].dev));
+    st = nvls_granularity(c->r[0].dev, c->n, &gran);
+    if (st != DT_OK) return st;
+    c->nvls_size = (bytes + gran - 1) / gran * gran;
+    CUmulticastObjectProp mp{};
+    mp.numDevices = static_cast<unsigned int>(c->n);
+    mp.size = c->nvls_size;
+    mp.handleTypes = 0;
+    DT_CU(D.mcCreate(&c->nvls_mc_handle, &mp));
+    c->nvls_have_mc = true;
+    int devs[kMaxRanks];
+    for (int r = 0; r < c->n; ++r) {
+        devs[r] = c->r[r].dev;
+        CUdevice cu = 0;
+        DT_CU(D.deviceGet(&cu, devs[r]));
+        DT_CU(D.mcAddDevice(c->nvls_mc_handle, cu));
+    }
+    for (int r = 0; r < c->n && st == DT_OK; ++r) {
+        DT_CUDA(cudaSetDevice(devs[r]));
+        st = nvls_bind_rank(c, r, devs, c->n);
+    }
+    if (st == DT_OK) st = nvls_map_multicast(c, devs, c->n, &c->nvls_mc_va);
+    if (st != DT_OK) {
+        const std::string msg = g_err;
+        nvls_release(c);
+        g_err = msg;
+        return st;
+    }
+    for (int r = 0; r < c->n; ++r) {
+        c->r[r].nvls_mc = reinterpret_cast<char*>(c->nvls_mc_va);
+        DT_CUDA(cudaSetDevice(devs[r]));
+        DT_CUDA(cudaMemset(c->r[r].nvls_uc, 0, c->nvls_size));
+        DT_CUDA(cudaDeviceSynchronize());
+    }
+    return DT_OK;
+}
+
+int dt_comm_nvls_create(dt_comm* c, size_t bytes, int* fd) {
+    DeviceGuard device_guard;
+    if (c == nullptr || fd == nullptr || bytes == 0 || !c->multiprocess)
+        return fail(DT_ERR_INVALID, "dt_comm_nvls_create needs a multi-process communicator, a size and an fd pointer");
+    if (c->nvls_have_mc) return fail(DT_ERR_STATE, "the communicator already has an NVLS buffer");
+    int supported = 0;
+    int st = dt_comm_nvls_supported(c, &supported);
+    if (st != DT_OK) return st;
+    if (!supported) return fail(DT_ERR_UNSUPPORTED, "NVLink multicast is not supported on this device");
+    const Driver& D = driver();
+    RankState& s = c->r[c->local_rank];
+    DT_CUDA(cudaSetDevice(s.dev));
+    size_t gran = 0;
+    st = nvls_granularity(s.dev, c->n, &gran);
+    if (st != DT_OK) return st;
+    c->nvls_size = (bytes + gran - 1) / gran * gran;
+    CUmulticastObjectProp mp{};
+    mp.numDevices = static_cast<unsigned int>(c->n);
+    mp.size = c->nvls_size;
+    mp.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+    DT_CU(D.mcCreate(&c->nvls_mc_handle, &mp));
+    c->nvls_have_mc = true;
+    int h = -1;
+    DT_CU(D.exportHandle(&h, c->nvls_mc_handle, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0));
+    *fd = h;
+    return DT_OK;
+}
+
+int dt_comm_nvls_attach(dt_comm* c, int fd, size_t bytes) {
+    DeviceGuard device_guard;
+    if (c == nullptr || bytes == 0 || !c->multiprocess) return fail(DT_ERR_INVALID, "dt_comm_nvls_attach: bad arguments");
+    const Driver& D = driver();
+    if (!D.ok) return fail(DT_ERR_UNSUPPORTED, "CUDA driver entry point missing: " + D.missing);
+    RankState& s = c->r[c->local_rank];
+    DT_CUDA(cudaSetDevice(s.dev));
+    size_t gran = 0;
+    int st = nvls_granularity(s.dev, c->n, &gran);
+    if (st != DT_OK) return st;
+    const size_t size = (bytes + gran - 1) / gran * gran;
+    if (!c->nvls_have_mc) {
+        if (fd < 0) return fail(DT_ERR_INVALID, "dt_comm_nvls_attach: invalid file descriptor");
+        DT_CU(D.importHandle(&c->nvls_mc_handle, reinterpret_cast<void*>(static_cast<uintptr_t>(fd)),
+                             CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR));
+        c->nvls_have_mc = true;
+        c->nvls_size = size;
+    } else if (c->nvls_size != size) {
+        return fail(DT_ERR_INVALID, "dt_comm_nvls_attach: size differs from the creator's");
+    }
+    CUdevice cu = 0;
+    DT_CU(D.deviceGet(&cu, s.dev));
+    DT_CU(D.mcAddDevice(c->nvls_mc_handle, cu));
+    return DT_OK;
+}
+
+int dt_comm_nvls_bind(dt_comm* c) {
+    DeviceGuard device_guard;
+    if (c == nullptr || !c->multiprocess || !c->nvls_have_mc)
+        return fail(DT_ERR_STATE, "dt_comm_nvls_bind: attach the multicast object first");
+    RankState& s = c->r[c->local_rank];
+    DT_CUDA(cudaSetDevice(s.dev));
+    const int dev = s.dev;
+    int st = nvls_bind_rank(c, c->local_rank, &dev, 1);
+    CUdeviceptr mc = 0;
+    if (st == DT_OK) st = nvls_map_multicast(c, &dev, 1, &mc);
+    if (st != DT_OK) return st;
+    s.nvls_mc = reinterpret_cast<char*>(mc);
+    DT_CUDA(cudaMemset(s.nvls_uc, 0, c->nvls_size));
+    DT_CUDA(cudaDeviceSynchronize());
+    return DT_OK;
+}
+
+int dt_comm_nvls_buffer(dt_comm* c, int rank, void** ptr, size_t* bytes) {
+    if (c == nullptr || !check_rank(c, rank) || ptr == nullptr || bytes == nullptr) return fail(DT_ERR_INVALID, "bad args");
+    *ptr = c->r[rank].nvls_uc;
+    *bytes = c->r[rank].nvls_uc != nullptr ? c->nvls_size : 0;
+    return DT_OK;
 }
 
 // ---- same-device kernels ----------------------------------------------------------------------------------

@@ -350,6 +350,84 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyA
     if (BARRIER) block_barrier(a.sig, a.bar_end);
 }
 
+// ------------------------------------------------------------------------------------------------------------
+// NVLS all-reduce: the buffers live in memory bound to one NVLink multicast object, so one multimem load
+// returns the sum of every rank's copy, reduced inside the NVSwitch (fp32 accumulation for bf16/fp16), and
+// one multimem store writes the result into every rank's copy. Rank c handles chunk c. Per GPU this moves
+// (1 + 1/n)·S each way instead of the two-shot's 2(n-1)/n·S; the summation order is the switch's, not rank
+// order (within the reductions' tolerance, not bit-identical to the rank-order fold).
+// ------------------------------------------------------------------------------------------------------------
+struct NvlsArgs {
+    SignalCtx sig;
+    const char* mc_in;  // multicast address of the input
+    char* mc_out;       // multicast address of the output
+    int64_t vlo, vhi;   // 16-byte vectors handled by this rank
+    uint32_t bar_start;
+    uint32_t bar_end;
+};
+
+template <int DT>
+__device__ __forceinline__ uint4 multimem_ld_reduce_v4(const void* p);
+
+template <>
+__device__ __forceinline__ uint4 multimem_ld_reduce_v4<0>(const void* p) {
+    uint4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+
+template <>
+__device__ __forceinline__ uint4 multimem_ld_reduce_v4<1>(const void* p) {
+    uint4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+
+template <>
+__device__ __forceinline__ uint4 multimem_ld_reduce_v4<2>(const void* p) {
+    uint4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+
+__device__ __forceinline__ void multimem_st_v4(void* p, const uint4& v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads) k_allreduce_nvls(const __grid_constant__ NvlsArgs a) {
+    if (!block_barrier(a.sig, a.bar_start)) return;
+    constexpr int U = 4;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x * U;
+    for (int64_t base = a.vlo + static_cast<int64_t>(blockIdx.x) * blockDim.x * U; base < a.vhi; base += step) {
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * blockDim.x + threadIdx.x;
+            if (v < a.vhi) r[u] = multimem_ld_reduce_v4<DT>(a.mc_in + v * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t v = base + u * blockDim.x + threadIdx.x;
+            if (v < a.vhi) multimem_st_v4(a.mc_out + v * 16, r[u]);
+        }
+    }
+    // the stores went through the multicast alias; peers read the same memory through their unicast mapping
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    block_barrier(a.sig, a.bar_end);
+}
+
 // Barrier-only kernel (ThreadGroup::Barrier): one block, both phases of the epoch.
 __global__ void k_barrier(const __grid_constant__ SignalCtx s, uint32_t v0, uint32_t v1) {
     if (block_barrier(s, v0)) block_barrier(s, v1);

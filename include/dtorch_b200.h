@@ -54,12 +54,16 @@ typedef enum dt_redop {
  *   DT_ACCUM_STORAGE  round to the storage type after every add, which is what the reference's CPU fold
  *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:224-228);
  *                     bit-identical to it. For fp32 both modes are the same left fold.
- *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size. */
+ *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size.
+ *   DT_ALGO_NVLS      reduce inside the NVSwitch (NVLink SHARP): needs input and output in the communicator's
+ *                     NVLS buffer (dt_comm_nvls_*); fp32 accumulation in the switch's order, not rank order.
+ *                     Picked by default for such buffers when the group has >= 4 ranks and >= 1 MiB. */
 #define DT_ACCUM_FP32 0x0
 #define DT_ACCUM_STORAGE 0x1
 #define DT_ALGO_AUTO 0x00
 #define DT_ALGO_ONESHOT 0x10
 #define DT_ALGO_TWOSHOT 0x20
+#define DT_ALGO_NVLS 0x40
 
 typedef struct dt_comm dt_comm;
 
@@ -155,6 +159,28 @@ int dt_all_to_all(dt_comm* comm, int rank, const void* in, void* out, int ndim, 
 
 /* Device-side barrier of all ranks on their streams. Replaces ThreadGroup::Barrier (thread_group.cc:118-125). */
 int dt_barrier(dt_comm* comm, int rank, void* stream);
+
+/* ---- NVLS buffer (NVLink SHARP) ------------------------------------------------------------------------- */
+/* Memory of every rank bound to one NVLink multicast object, so an all-reduce can reduce inside the NVSwitch
+ * (dt_all_reduce with DT_ALGO_NVLS). Buffers at the same offset on every rank form one operand. No
+ * counterpart in the reference, whose GPU collectives are NCCL's. */
+
+/* *supported = 1 if every local device of the communicator supports NVLink multicast. */
+int dt_comm_nvls_supported(dt_comm* comm, int* supported);
+
+/* Single-process peer communicator: allocate `bytes` (rounded up to the multicast granularity) per rank. */
+int dt_comm_nvls_alloc(dt_comm* comm, size_t bytes);
+
+/* Multi-process communicator, three steps: one rank creates the multicast object and exports it as a POSIX
+ * file descriptor (*fd) that the caller hands to the other processes (e.g. SCM_RIGHTS); then every rank
+ * calls dt_comm_nvls_attach (the creator with any fd) to add its device; after every rank has attached,
+ * every rank calls dt_comm_nvls_bind to bind and map its memory. The caller closes received descriptors. */
+int dt_comm_nvls_create(dt_comm* comm, size_t bytes, int* fd);
+int dt_comm_nvls_attach(dt_comm* comm, int fd, size_t bytes);
+int dt_comm_nvls_bind(dt_comm* comm);
+
+/* Rank `rank`'s pointer to its NVLS buffer and the buffer size (NULL / 0 if none). */
+int dt_comm_nvls_buffer(dt_comm* comm, int rank, void** ptr, size_t* bytes);
 
 /* ---- same-device kernels: all n ranks' buffers on the current device, one launch ------------------------- */
 /* These are the kernels a same-device communicator launches; they are exported so a caller that already holds

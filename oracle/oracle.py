@@ -190,6 +190,9 @@ class Reference:
     def all_to_all(self, ins, dtype: int, src_dim: int, dst_dim: int, iters: int = 1, threads: int = 0):
         ins = [_contig(a, dtype) for a in ins]
         n, ndim = len(ins), ins[0].ndim
+        if ins[0].shape[dst_dim] < n:
+            # the reference asserts shapeSize >= numShard (distributed_spec.cc:203) and its harness would exit
+            raise ValueError("all-to-all: destination extent smaller than the group")
         shapes = [s for a in ins for s in a.shape]
         split = shard_sizes(ins[0].shape[dst_dim], n)
         outs = []

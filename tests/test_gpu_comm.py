@@ -218,3 +218,68 @@ def test_same_device_rendezvous_times_out_cleanly():
         assert ei.value.status == capi.DT_ERR_STATE  # broken communicator refuses further calls
     finally:
         comm.destroy()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_nvls_all_reduce(dtype):
+    """NVLS all-reduce (reduction inside the NVSwitch): within the north-star tolerance of the rank-order
+    fold, identical on every rank and from run to run; in place; picked by default for NVLS buffers at
+    >= 4 ranks and >= 1 MiB."""
+    n = min(ngpu(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    devs = list(range(n))
+    comm = capi.Comm(devs)
+    try:
+        if not comm.nvls_supported():
+            pytest.skip("NVLink multicast not supported here")
+        es = torch.tensor([], dtype=dtype).element_size()
+        count = (1 << 20) + 64 // es  # multiple of 16 bytes, not of a power of two
+        comm.nvls_alloc(2 * count * es + (1 << 20))
+        code = capi.dtype_code(dtype)
+        name = {torch.bfloat16: "bfloat16", torch.float32: "float32"}[dtype]
+        g = torch.Generator().manual_seed(7)
+        host = [torch.randn(count, generator=g).to(dtype) for _ in range(n)]
+        xs, ys = [], []
+        for r in range(n):
+            base, size = comm.nvls_buffer(r)
+            assert size >= 2 * count * es
+            x = view_device_memory(base, count, dtype, r)
+            y = view_device_memory(base + count * es + 4096, count, dtype, r)
+            x.copy_(host[r].to(f"cuda:{r}"))
+            xs.append(x)
+            ys.append(y)
+        torch.cuda.synchronize()
+        want = R.fold_sum([raw_from_torch(h) for h in host], DT_CODE[name], storage_round=False)
+
+        def run(flags, in_place=False):
+            def fn(r):
+                with torch.cuda.device(r):
+                    s = torch.cuda.current_stream(r)
+                    dst = xs[r] if in_place else ys[r]
+                    comm.all_reduce(r, xs[r].data_ptr(), dst.data_ptr(), count, code, flags, s.cuda_stream)
+                    s.synchronize()
+            run_ranks(n, fn)
+
+        run(capi.DT_ALGO_NVLS)
+        first = [np_raw(y) for y in ys]
+        run(capi.DT_ALGO_NVLS)
+        for r in range(n):
+            assert np.array_equal(np_raw(ys[r]), first[r]), "run-to-run"
+            assert np.array_equal(first[r], first[0]), "ranks disagree"
+            assert_close(first[r], want, name)
+        assert comm.error(0) == capi.DT_OK
+        if n >= 4:  # default algorithm on NVLS buffers
+            for y in ys:
+                y.zero_()
+            torch.cuda.synchronize()
+            run(0)
+            assert np.array_equal(np_raw(ys[0]), first[0])
+        run(capi.DT_ALGO_NVLS, in_place=True)
+        for r in range(n):
+            assert np.array_equal(np_raw(xs[r]), first[0])
+        with pytest.raises(capi.DtError):  # storage rounding is not available in the switch
+            comm.all_reduce(0, xs[0].data_ptr(), ys[0].data_ptr(), count, code,
+                            capi.DT_ALGO_NVLS | capi.DT_ACCUM_STORAGE, 0)
+    finally:
+        comm.destroy()

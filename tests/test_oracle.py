@@ -81,7 +81,7 @@ def test_restatement_matches_live_reference(n):
         outs, _ = ref.all_reduce(ins, code)
         assert np.array_equal(R.fold_sum(ins, code, True).reshape(-1), outs[0])
         lens = shard_sizes(3 * n + 5, n)
-        parts = [raw_from_torch(torch.randn(l, 6, generator=g).to(dt)) for l in lens]
+        parts = [raw_from_torch(torch.randn(l, 2 * n + 3, generator=g).to(dt)) for l in lens]
         outs, _ = ref.all_to_all(parts, code, 0, 1)
         for a, b in zip(R.all_to_all(parts, 0, 1), outs):
             assert np.array_equal(a, b)
