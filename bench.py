@@ -809,7 +809,7 @@ def run_sweep_multi(args, rank, world, local_rank):
                     else:
                         dist.all_to_all_single(ya, xa)
 
-                impls = [("ours", ours), ("nccl", nccl)]
+                impls = [("ours", ours)] + ([] if args.sweep_no_nccl else [("nccl", nccl)])
                 if op == "all_reduce" and nvls_base and (in_n * es) % 16 == 0:
                     xn = heap_tensor(nvls_base, 0, in_n, dtype, dev)
                     yn = heap_tensor(nvls_base, max_bytes + (2 << 20), out_n, dtype, dev)
@@ -842,10 +842,11 @@ def run_sweep_multi(args, rank, world, local_rank):
                 busf = bus_factor(op, n)
                 msg = in_n * es if op != "all_gather" else out_n * es
                 if rank == 0:
+                    nccl_ms = res.get("nccl", float("nan"))
                     line = {"sweep": op, "n_gpus": n, "dtype": DT_NAME[dtype], "bytes": msg,
-                            "ours_ms": round(res["ours"], 5), "nccl_ms": round(res["nccl"], 5),
+                            "ours_ms": round(res["ours"], 5), "nccl_ms": round(nccl_ms, 5),
                             "ours_bus_gbs": round(msg * busf / res["ours"] / 1e6, 2),
-                            "nccl_bus_gbs": round(msg * busf / res["nccl"] / 1e6, 2),
+                            "nccl_bus_gbs": round(msg * busf / nccl_ms / 1e6, 2),
                             "device_error": comm.error(rank)}
                     if "nvls" in res:
                         line["nvls_ms"] = round(res["nvls"], 5)
@@ -1008,6 +1009,7 @@ def main():
     p.add_argument("--sweep-lo", type=int, default=10, help="smallest size, log2 bytes")
     p.add_argument("--sweep-hi", type=int, default=30, help="largest size, log2 bytes")
     p.add_argument("--sweep-ops", default="all_reduce,all_gather,reduce_scatter,all_to_all")
+    p.add_argument("--sweep-no-nccl", action="store_true", help="sweep without the NCCL comparison")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

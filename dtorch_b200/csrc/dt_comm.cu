@@ -301,6 +301,17 @@ int pick_grid(K kernel, int dev, int num_sms, int64_t want_blocks, int per_sm_ca
 constexpr int kReduceBlocksPerSM = 2;
 constexpr int kCopyBlocksPerSM = 2;
 
+// Upper bound on the CTAs of a peer (cross-GPU) launch; DTORCH_B200_P2P_CTAS overrides the default (no cap
+// beyond the residency limit). Every rank must use the same value.
+int64_t p2p_ctas() {
+    static const int64_t v = [] {
+        const char* s = std::getenv("DTORCH_B200_P2P_CTAS");
+        const long long x = (s != nullptr && *s != '\0') ? std::atoll(s) : 0;
+        return x > 0 ? static_cast<int64_t>(std::min<long long>(x, kMaxBlocks)) : static_cast<int64_t>(kMaxBlocks);
+    }();
+    return v;
+}
+
 template <int NR>
 constexpr int reduce_unroll() { return NR <= 2 ? 4 : 2; }
 
@@ -315,6 +326,7 @@ template <int DT, int NR, bool ST, bool BAR>
 int launch_reduce_t(const ReduceArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks) {
     auto k = k_reduce<DT, NR, ST, BAR>;
     if (want_blocks <= 0) want_blocks = reduce_want_blocks(a.vhi - a.vlo, a.shi - a.slo, NR);
+    if (BAR) want_blocks = std::min(want_blocks, p2p_ctas());
     int grid = 1;
     pick_grid(k, dev, num_sms, want_blocks, kReduceBlocksPerSM, &grid);
     k<<<grid, kThreads, 0, stream>>>(a);
@@ -440,12 +452,19 @@ int launch_copy_t(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream
         a.max_items = std::max(a.max_items, s.items);
     }
     auto k = k_copy<VW, MAXSEG, BAR>;
+    int per_sm = kCopyBlocksPerSM;
+    if (BAR && want_blocks > 0) {
+        // peer copies, measured at 8 GPUs: one CTA per SM keeps the fabric less congested up to ~256 MiB
+        // per rank; two per SM win a few percent above (the size measure is the same on every rank)
+        if (want_blocks < 16384) per_sm = 1;
+        want_blocks = std::min(want_blocks, p2p_ctas());
+    }
     if (want_blocks <= 0) {
         const int64_t warps_per_block = kThreads / 32;
         want_blocks = std::max<int64_t>((a.max_items * a.nseg + warps_per_block - 1) / warps_per_block, 1);
     }
     int grid = 1;
-    pick_grid(k, dev, num_sms, want_blocks, kCopyBlocksPerSM, &grid);
+    pick_grid(k, dev, num_sms, want_blocks, per_sm, &grid);
     k<<<grid, kThreads, 0, stream>>>(a);
     return launch_check("k_copy");
 }
@@ -767,8 +786,21 @@ void nvls_release(dt_comm* c) {
     c->nvls_size = 0;
 }
 
+// CTAs issuing multimem traffic per rank. The switch serves a bounded number of in-flight reductions; more
+// CTAs than that only queue up (measured: fewer CTAs keep NVLS throughput steady as messages grow).
+// DTORCH_B200_NVLS_CTAS overrides the default; every rank must use the same value.
+int64_t nvls_ctas() {
+    static const int64_t v = [] {
+        const char* s = std::getenv("DTORCH_B200_NVLS_CTAS");
+        const long long x = (s != nullptr && *s != '\0') ? std::atoll(s) : 0;
+        return x > 0 ? static_cast<int64_t>(std::min<long long>(x, kMaxBlocks)) : static_cast<int64_t>(16);
+    }();
+    return v;
+}
+
 template <int DT>
 int launch_nvls_t(const NvlsArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want) {
+    want = std::min(want, nvls_ctas());
     auto k = k_allreduce_nvls<DT>;
     int grid = 1;
     pick_grid(k, dev, num_sms, want, kReduceBlocksPerSM, &grid);
@@ -1081,8 +1113,9 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
         if (want_nvls && storage)
             return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NVLS reduces in the switch with fp32 accumulation; "
                                             "DT_ACCUM_STORAGE is not available with it");
+        // measured at 8 ranks: NVLS ahead of the two-shot kernel from 8-16 MiB up; not measured below 6 ranks
         const bool auto_nvls = (flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT | DT_ALGO_NVLS)) == 0 && nvls_ok && !storage &&
-                               c->n >= 4 && bytes >= (static_cast<size_t>(1) << 20);
+                               c->n >= 6 && bytes >= (static_cast<size_t>(8) << 20);
         if (want_nvls || auto_nvls) {
             NvlsArgs na{};
             const uint32_t epoch = ++s.epoch;
