@@ -11,7 +11,7 @@
 __version__ = "0.1.0"
 
 _DTENSOR_NAMES = ("DeviceMesh", "Placement", "Shard", "Replicate", "Partial", "init_device_mesh", "DTensor",
-                  "cuda_device_of", "clear")
+                  "cuda_device_of", "clear", "redistribute_many", "reduce")
 
 
 def __getattr__(name):
@@ -19,4 +19,8 @@ def __getattr__(name):
         from . import dtensor
 
         return getattr(dtensor, name)
+    if name == "scaled_dot_product_attention_with_cp":
+        from . import context_parallel
+
+        return context_parallel.scaled_dot_product_attention_with_cp
     raise AttributeError(name)

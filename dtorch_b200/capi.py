@@ -64,6 +64,7 @@ SIGNATURES = [
     ("dt_local_all_gather", _I, [_I, _P, _P, _SZ, _P, _SZ, _P]),
     ("dt_local_all_to_all", _I, [_I, _P, _P, _I, _P, _I, _I, _P, _SZ, _P]),
     ("dt_kernel_launch_count", ctypes.c_uint64, []),
+    ("dt_all_to_all_multi", _I, [_P, _I, _I, _P, _P, _I, _P, _I, _I, _P, _SZ, _P]),
     ("dt_comm_nvls_supported", _I, [_P, _P]),
     ("dt_comm_nvls_alloc", _I, [_P, _SZ]),
     ("dt_comm_nvls_create", _I, [_P, _SZ, _P]),
@@ -242,6 +243,11 @@ class Comm:
     def all_to_all(self, rank, inp, out, in_shape, src_dim, dst_dim, src_lens, elem_bytes, stream=0):
         check(lib().dt_all_to_all(self._h, rank, inp, out, len(in_shape), i64_array(in_shape), src_dim, dst_dim,
                                   i64_array(src_lens), elem_bytes, stream), "dt_all_to_all")
+
+    def all_to_all_multi(self, rank, ins, outs, in_shape, src_dim, dst_dim, src_lens, elem_bytes, stream=0):
+        check(lib().dt_all_to_all_multi(self._h, rank, len(ins), ptr_array(ins), ptr_array(outs), len(in_shape),
+                                        i64_array(in_shape), src_dim, dst_dim, i64_array(src_lens), elem_bytes, stream),
+              "dt_all_to_all_multi")
 
     def barrier(self, rank, stream=0):
         check(lib().dt_barrier(self._h, rank, stream), "dt_barrier")

@@ -1,0 +1,74 @@
+"""Context-parallel scaled-dot-product attention over DTensors (the reference's
+python/dtorch/nn/scaled_dot_product_attention_with_cp.py:14-111, Ulysses and "ring" paths).
+
+Layout (N, H, L, E); q, k and v are sharded on the sequence (Shard(2)) along the context-parallel mesh dims.
+
+* Ulysses: the sequence-sharded q, k, v become head-sharded (Shard(2) -> Shard(1)) in ONE fused all-to-all
+  launch per device (the reference issues three redistributes), each device runs attention for its heads over
+  the whole sequence, and the output returns to Shard(2).
+* "Ring" (as the reference implements it): K and V are all-gathered along the ring dim (Shard(2) ->
+  Replicate) and each device attends its query chunk to the whole key/value sequence (non-causal only here).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Union
+
+import torch
+import torch.nn.functional as F
+
+from .dtensor import DTensor, Replicate, Shard, redistribute_many
+
+
+def _dim_index(tensor: DTensor, dim: Optional[Union[int, str]]) -> Optional[int]:
+    if dim is None:
+        return None
+    if isinstance(dim, str):
+        if dim not in tensor.device_mesh.dim_names:
+            return None
+        dim = tensor.device_mesh.dim_names.index(dim)
+    return None if tensor.device_mesh.shape[dim] == 1 else dim
+
+
+def scaled_dot_product_attention_with_cp(query: DTensor, key: DTensor, value: DTensor, dropout_p: float = 0.0,
+                                         is_causal: bool = False, scale: Optional[float] = None,
+                                         ulysses_cp_dim: Optional[Union[int, str]] = None,
+                                         ring_cp_dim: Optional[Union[int, str]] = None) -> DTensor:
+    u = _dim_index(query, ulysses_cp_dim)
+    r = _dim_index(query, ring_cp_dim)
+    if key.placements != query.placements or value.placements != query.placements:
+        raise RuntimeError("query, key and value have different placements")
+    for d in (u, r):
+        if d is not None and query.placements[d] != Shard(2):
+            raise ValueError("context-parallel dims must shard the sequence dim (Shard(2))")
+    if r is not None and is_causal:
+        raise NotImplementedError("causal attention with an all-gathered (ring) K/V needs the sub-split layout")
+    mesh = query.device_mesh
+    placements = list(query.placements)
+    if u is not None:
+        n = mesh.shape[u]
+        if query.shape[1] % n or key.shape[1] % n:
+            raise ValueError(f"attention heads ({query.shape[1]}, {key.shape[1]}) cannot be divided evenly by the "
+                             f"Ulysses size {n}")
+        head = list(placements)
+        head[u] = Shard(1)
+        if query.shape == key.shape == value.shape:
+            query, key, value = redistribute_many([query, key, value], head)
+        else:
+            query = query.redistribute(placements=head)
+            key, value = redistribute_many([key, value], head)
+    if r is not None:
+        kv = list(query.placements)
+        kv[r] = Replicate()
+        key, value = redistribute_many([key, value], kv)
+    out_locals = {}
+    for gid in mesh.ids:
+        q, k, v = query.local(gid), key.local(gid), value.local(gid)
+        with torch.cuda.device(q.device):
+            out_locals[gid] = F.scaled_dot_product_attention(q, k, v, dropout_p=dropout_p, is_causal=is_causal,
+                                                             scale=scale)
+    out_shape = tuple(query.shape[:3]) + (value.shape[3],)
+    out = DTensor(out_locals, mesh, query.placements, out_shape)
+    if u is not None:
+        return out.redistribute(placements=placements)
+    return out

@@ -111,6 +111,7 @@ struct Slot {
     const void* in;
     void* out;
     cudaStream_t stream;
+    void* extra[kMaxRanks];  // further outputs of a multi-tensor call, copied by value
 };
 
 }  // namespace
@@ -1390,6 +1391,92 @@ int dt_all_to_all(dt_comm* c, int rank, const void* in, void* out, int ndim, con
     const int64_t rows = g.d0 * g.dmid * (g.src_first ? max_l : max_k);
     const int64_t want = copy_want_blocks(run, rows, c->n);
     return launch_copy<kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+}
+
+int dt_all_to_all_multi(dt_comm* c, int rank, int ntensors, const void* const* ins_v, void* const* outs_v, int ndim,
+                        const int64_t* in_shape, int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_b,
+                        void* stream_v) {
+    DeviceGuard device_guard;
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    if (ntensors < 1 || ntensors > kMaxRanks || ins_v == nullptr || outs_v == nullptr)
+        return fail(DT_ERR_INVALID, "dt_all_to_all_multi: ntensors must be 1..8");
+    if (ntensors == 1)
+        return dt_all_to_all(c, rank, ins_v[0], outs_v[0], ndim, in_shape, src_dim, dst_dim, src_lens, elem_b, stream_v);
+    A2AGeom g{};
+    st = a2a_geom(c->n, ndim, in_shape, src_dim, dst_dim, src_lens, elem_b, &g);
+    if (st != DT_OK) return st;
+    if (in_shape[src_dim] != src_lens[rank]) return fail(DT_ERR_INVALID, "a2a: in_shape[src_dim] != src_lens[rank]");
+    int64_t split[kMaxRanks], doff[kMaxRanks], soff[kMaxRanks];
+    shard_sizes(g.D, c->n, split);
+    int64_t acc = 0;
+    for (int k = 0; k < c->n; ++k) {
+        doff[k] = acc;
+        acc += split[k];
+    }
+    acc = 0;
+    for (int r = 0; r < c->n; ++r) {
+        soff[r] = acc;
+        acc += src_lens[r];
+    }
+    const int64_t in_elems = g.d0 * g.dmid * g.d2 * g.D * src_lens[rank];
+    const int64_t out_elems = g.d0 * g.dmid * g.d2 * g.A * split[rank];
+    for (int t = 0; t < ntensors; ++t)
+        if ((in_elems > 0 && ins_v[t] == nullptr) || (out_elems > 0 && outs_v[t] == nullptr))
+            return fail(DT_ERR_INVALID, "null buffer");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    if (c->same_device || c->n == 1) {
+        for (int t = 0; t < ntensors; ++t) {
+            st = dt_all_to_all(c, rank, ins_v[t], outs_v[t], ndim, in_shape, src_dim, dst_dim, src_lens, elem_b, stream_v);
+            if (st != DT_OK) return st;
+        }
+        return DT_OK;
+    }
+    DT_CUDA(cudaSetDevice(s.dev));
+    // every rank's output pointers of every tensor, as addressed from this device
+    char* outs[kMaxRanks][kMaxRanks];  // [tensor][rank]
+    bool heap = true;
+    for (int t = 0; t < ntensors; ++t)
+        heap = heap && in_heap(c, rank, outs_v[t], static_cast<size_t>(out_elems) * elem_b);
+    if (heap) {
+        for (int t = 0; t < ntensors; ++t) {
+            const ptrdiff_t o = static_cast<char*>(outs_v[t]) - s.heap;
+            for (int r = 0; r < c->n; ++r) outs[t][r] = s.peer_heap[r] + o;
+        }
+    } else if (c->multiprocess) {
+        return fail(DT_ERR_INVALID, "multi-process communicator: buffers must live in the symmetric heap");
+    } else {
+        Slot mine{};
+        mine.in = ins_v[0];
+        mine.out = outs_v[0];
+        for (int t = 0; t < ntensors; ++t) mine.extra[t] = outs_v[t];
+        Slot all[kMaxRanks];
+        st = rendezvous(c, rank, mine, all);
+        if (st != DT_OK) return st;
+        for (int t = 0; t < ntensors; ++t)
+            for (int r = 0; r < c->n; ++r) outs[t][r] = static_cast<char*>(all[r].extra[t]);
+    }
+    CopyArgs<kMaxRanks * kMaxRanks> a{};
+    const uint32_t epoch = ++s.epoch;
+    a.sig = make_sig(c, rank);
+    a.bar_start = 2 * epoch - 1;
+    a.bar_end = 2 * epoch;
+    a.nseg = ntensors * c->n;
+    // segment (j * ntensors + t): tensor t to destination (rank + 1 + j) % n -- destinations interleaved
+    for (int j = 0; j < c->n; ++j) {
+        const int k = (rank + 1 + j) % c->n;
+        for (int t = 0; t < ntensors; ++t)
+            a.seg[j * ntensors + t] = a2a_seg(g, static_cast<const char*>(ins_v[t]), outs[t][k], src_lens[rank],
+                                              soff[rank], split[k], doff[k]);
+    }
+    int64_t max_l = 0;
+    for (int r = 0; r < c->n; ++r) max_l = std::max(max_l, src_lens[r]);
+    const int64_t max_k = split[0];
+    const int64_t run = (g.src_first ? max_k : max_l) * g.d2 * g.es;
+    const int64_t rows = g.d0 * g.dmid * (g.src_first ? max_l : max_k);
+    const int64_t want = copy_want_blocks(run, rows, c->n * ntensors);
+    return launch_copy<kMaxRanks * kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
 }
 
 int dt_barrier(dt_comm* c, int rank, void* stream_v) {

@@ -62,6 +62,10 @@ PYBIND11_MODULE(_host, m) {
              [](ThreadGroup& g, const torch::Tensor& x, size_t src, size_t dst,
                 const std::map<int64_t, std::vector<int64_t>>& s) { return g.AllToAll(x, src, dst, Shapes(s)); },
              py::call_guard<py::gil_scoped_release>())
+        .def("all_to_all_multi",
+             [](ThreadGroup& g, const std::vector<torch::Tensor>& xs, size_t src, size_t dst,
+                const std::map<int64_t, std::vector<int64_t>>& s) { return g.AllToAllMulti(xs, src, dst, Shapes(s)); },
+             py::call_guard<py::gil_scoped_release>())
         .def("replicate_to_shard", &ThreadGroup::ReplicateToShard, py::arg("input"), py::arg("shard_idx"),
              py::arg("sub_split_coordinates") = -1, py::call_guard<py::gil_scoped_release>());
 
@@ -81,6 +85,14 @@ PYBIND11_MODULE(_host, m) {
              const std::vector<int64_t>& meshIds, const std::vector<std::string>& src, const std::vector<std::string>& dst,
              const std::vector<int64_t>& globalShape) {
               return Redistribute(locals, Mesh(meshShape, meshIds), ParseSeq(src), ParseSeq(dst), globalShape);
+          },
+          py::call_guard<py::gil_scoped_release>());
+
+    m.def("redistribute_multi",
+          [](const std::vector<std::map<int64_t, torch::Tensor>>& locals, const std::vector<int64_t>& meshShape,
+             const std::vector<int64_t>& meshIds, const std::vector<std::string>& src, const std::vector<std::string>& dst,
+             const std::vector<int64_t>& globalShape) {
+              return RedistributeMulti(locals, Mesh(meshShape, meshIds), ParseSeq(src), ParseSeq(dst), globalShape);
           },
           py::call_guard<py::gil_scoped_release>());
 

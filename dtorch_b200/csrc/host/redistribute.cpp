@@ -197,4 +197,64 @@ std::map<int64_t, torch::Tensor> Redistribute(const std::map<int64_t, torch::Ten
     return cur;
 }
 
+std::vector<std::map<int64_t, torch::Tensor>> RedistributeMulti(const std::vector<std::map<int64_t, torch::Tensor>>& locals,
+                                                                const DeviceMesh& mesh, PlacementSeq src, PlacementSeq dst,
+                                                                const std::vector<int64_t>& globalShape) {
+    ShardDimToPositive(src, globalShape.size());
+    ShardDimToPositive(dst, globalShape.size());
+    ToReplicateWhenDimSizeEqualOne(src, mesh);
+    ToReplicateWhenDimSizeEqualOne(dst, mesh);
+    const auto diff = GetDiffDims(src, dst);
+    const bool fused = locals.size() > 1 && locals.size() <= 8 && diff.size() == 1 && src[diff[0]].IsShard() &&
+                       dst[diff[0]].IsShard() && !src[diff[0]].HasSubSplit() && !dst[diff[0]].HasSubSplit();
+    if (!fused) {
+        std::vector<std::map<int64_t, torch::Tensor>> out;
+        for (const auto& l : locals) out.push_back(Redistribute(l, mesh, src, dst, globalShape));
+        return out;
+    }
+    CheckValid(globalShape, mesh, src);
+    CheckValid(globalShape, mesh, dst);
+    const size_t d = diff[0];
+    LocalShapes operand;
+    operand.shapes = ComputeLocalShapes(globalShape, mesh, src);
+    std::vector<std::map<int64_t, torch::Tensor>> out(locals.size());
+    std::map<int64_t, std::future<void>> futs;
+    std::mutex out_mu;
+    for (auto id : mesh.ids) {
+        auto& ks = KernelStreamManager::Global().Get(id);
+        std::vector<torch::Tensor> ins;
+        for (const auto& l : locals) ins.push_back(l.at(id));
+        auto ev = std::make_shared<at::cuda::CUDAEvent>();
+        ev->record(c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice())));
+        futs[id] = ks.Launch([&, ins, ev, id]() {
+            auto stream = c10::cuda::getCurrentCUDAStream();
+            ev->block(stream);
+            for (const auto& t : ins) c10::cuda::CUDACachingAllocator::recordStream(t.storage().data_ptr(), stream);
+            const auto group = GroupDeviceIds(mesh, d, id);
+            ThreadGroup& tg = ThreadGroupManager::Global().GetThreadGroup(group, id);
+            auto r = tg.AllToAllMulti(ins, static_cast<size_t>(src[d].dim), static_cast<size_t>(dst[d].dim), operand);
+            std::lock_guard<std::mutex> g(out_mu);
+            for (size_t t = 0; t < r.size(); ++t) out[t][id] = r[t];
+        });
+    }
+    std::exception_ptr err;
+    for (auto& kv : futs) {
+        try {
+            kv.second.get();
+        } catch (...) {
+            if (!err) err = std::current_exception();
+        }
+    }
+    if (err) std::rethrow_exception(err);
+    for (auto id : mesh.ids) {
+        auto& ks = KernelStreamManager::Global().Get(id);
+        auto caller = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice()));
+        at::cuda::CUDAEvent done;
+        done.record(ks.Stream());
+        done.block(caller);
+        for (auto& o : out) c10::cuda::CUDACachingAllocator::recordStream(o.at(id).storage().data_ptr(), caller);
+    }
+    return out;
+}
+
 }  // namespace dtb

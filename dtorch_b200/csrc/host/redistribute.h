@@ -75,4 +75,11 @@ torch::Tensor ConvertPlacements(const torch::Tensor& input, const DeviceMesh& me
 std::map<int64_t, torch::Tensor> Redistribute(const std::map<int64_t, torch::Tensor>& locals, const DeviceMesh& mesh,
                                               PlacementSeq src, PlacementSeq dst, const std::vector<int64_t>& globalShape);
 
+// Redistribute several DTensors of one shape and placement the same way. A change of one mesh dim from
+// Shard(i) to Shard(j) runs as one fused all-to-all launch per device for all of them (the q/k/v swap of
+// Ulysses context parallelism); anything else runs Redistribute per tensor.
+std::vector<std::map<int64_t, torch::Tensor>> RedistributeMulti(const std::vector<std::map<int64_t, torch::Tensor>>& locals,
+                                                                const DeviceMesh& mesh, PlacementSeq src, PlacementSeq dst,
+                                                                const std::vector<int64_t>& globalShape);
+
 }  // namespace dtb

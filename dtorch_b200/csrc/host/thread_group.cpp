@@ -297,6 +297,40 @@ torch::Tensor ThreadGroup::AllToAll(const torch::Tensor& input, size_t srcDim, s
     return out;
 }
 
+std::vector<torch::Tensor> ThreadGroup::AllToAllMulti(const std::vector<torch::Tensor>& inputs, size_t srcDim,
+                                                      size_t destDim, const LocalShapes& operand) {
+    TORCH_CHECK(!inputs.empty() && inputs.size() <= 8, "AllToAllMulti: 1..8 tensors");
+    std::vector<torch::Tensor> ins;
+    for (const auto& t : inputs) {
+        CheckInput(t);
+        TORCH_CHECK(t.sizes() == inputs[0].sizes() && t.scalar_type() == inputs[0].scalar_type(),
+                    "AllToAllMulti: tensors must share shape and dtype");
+        ins.push_back(t.contiguous());
+    }
+    auto shape = ins[0].sizes().vec();
+    TORCH_CHECK(srcDim < shape.size() && destDim < shape.size() && srcDim != destDim, "AllToAllMulti: bad dims");
+    std::vector<int64_t> srcLens;
+    for (auto id : mIds) srcLens.push_back(operand.Get(id)[srcDim]);
+    TORCH_CHECK(srcLens[static_cast<size_t>(mRank)] == shape[srcDim], "AllToAllMulti: local shape disagrees with the operand");
+    auto out_shape = shape;
+    out_shape[srcDim] = std::accumulate(srcLens.begin(), srcLens.end(), int64_t{0});
+    out_shape[destDim] = ShardSizes(shape[destDim], mSize)[static_cast<size_t>(mRank)];
+    std::vector<torch::Tensor> outs;
+    std::vector<const void*> in_ptrs;
+    std::vector<void*> out_ptrs;
+    for (auto& t : ins) {
+        outs.push_back(torch::empty(out_shape, t.options()));
+        in_ptrs.push_back(t.data_ptr());
+        out_ptrs.push_back(outs.back().data_ptr());
+    }
+    Check(dt_all_to_all_multi(mComm->get(), mRank, static_cast<int>(ins.size()), in_ptrs.data(), out_ptrs.data(),
+                              static_cast<int>(shape.size()), shape.data(), static_cast<int>(srcDim),
+                              static_cast<int>(destDim), srcLens.data(), static_cast<size_t>(ins[0].element_size()),
+                              Stream()),
+          "dt_all_to_all_multi");
+    return outs;
+}
+
 torch::Tensor ThreadGroup::ReplicateToShard(const torch::Tensor& input, int64_t shardIdx, int64_t subSplitCoordinates) {
     TORCH_CHECK(shardIdx >= 0 && shardIdx < input.dim(), "ReplicateToShard: shard dim out of range");
     const int64_t len = input.size(shardIdx);

@@ -105,6 +105,9 @@ public:
     torch::Tensor ReduceScatterTensor(const torch::Tensor& input, ReduceOpType op = ReduceOpType::kSum);
     // S(srcDim) -> S(destDim); the split/contiguous pack and the concat happen inside the kernel
     torch::Tensor AllToAll(const torch::Tensor& input, size_t srcDim, size_t destDim, const LocalShapes& operand);
+    // the same S(srcDim) -> S(destDim) for several tensors of one shape, in one launch
+    std::vector<torch::Tensor> AllToAllMulti(const std::vector<torch::Tensor>& inputs, size_t srcDim, size_t destDim,
+                                             const LocalShapes& operand);
     // R -> S(shardIdx); subSplitCoordinates < 0 means a plain shard
     torch::Tensor ReplicateToShard(const torch::Tensor& input, int64_t shardIdx, int64_t subSplitCoordinates = -1);
 

@@ -239,3 +239,55 @@ class DTensor:
 def clear() -> None:
     """Destroy the kernel-stream threads and communicators (e.g. before switching device-mapping modes)."""
     _host.clear()
+
+
+def redistribute_many(tensors: Sequence[DTensor], placements: Sequence[Placement]) -> List[DTensor]:
+    """Redistribute DTensors of one shape, mesh and placement to the same new placements. When the change is
+    Shard(i) -> Shard(j) on one mesh dim, all of them move in one fused all-to-all launch per device."""
+    first = tensors[0]
+    for t in tensors[1:]:
+        if t.shape != first.shape or t.placements != first.placements or t.device_mesh != first.device_mesh:
+            raise ValueError("redistribute_many: tensors differ in shape, placements or mesh")
+    mesh = first.device_mesh
+    outs = _host.redistribute_multi([t._locals for t in tensors], list(mesh.shape), mesh.ids,
+                                    _strings(first.placements), _strings(placements), list(first.shape))
+    normalized = _host.normalize(_strings(placements), list(mesh.shape), mesh.ids, len(first.shape))
+    return [DTensor(o, mesh, [Placement(p) for p in normalized], first.shape) for o in outs]
+
+
+def reduce(tensor: DTensor, dims: Union[int, Sequence[int]], kind: str = "sum", keepdim: bool = False) -> DTensor:
+    """Sum or mean over tensor dims of a DTensor (the reference's ReduceKernel::Compute,
+    dtorch/core/kernel/kernel_implement/reduce_kernel.cc:63-116). Each device reduces its shard; a mesh dim that
+    sharded a reduced dim leaves the result Partial, and one all-reduce per such mesh dim (rank-order fp32 fold)
+    makes it Replicate -- instead of the reference's all-gather of every rank's partial and a host-side fold,
+    which moves n times the data. `mean` divides the global sum by the global element count (for uneven shards
+    the reference's mean of per-rank means is not the mean)."""
+    if kind not in ("sum", "mean"):
+        raise ValueError("kind must be 'sum' or 'mean'")
+    nd = len(tensor.shape)
+    dims = [dims] if isinstance(dims, int) else list(dims)
+    dims = sorted({d % nd for d in dims})
+    if any(p.is_partial() for p in tensor.placements):
+        raise ValueError("reduce of a Partial DTensor: redistribute it first")
+    locals_ = {gid: t.sum(dim=dims, keepdim=keepdim) for gid, t in tensor._locals.items()}
+    placements, to_replicate = [], []
+    for p in tensor.placements:
+        if p.is_shard() and p.get_shard_index() in dims:
+            placements.append(Partial())
+            to_replicate.append(Replicate())
+        elif p.is_shard() and not keepdim:
+            d = p.get_shard_index()
+            placements.append(Shard(d - sum(1 for r in dims if r < d)))
+            to_replicate.append(placements[-1])
+        else:
+            placements.append(p)
+            to_replicate.append(p)
+    shape = [1 if i in dims else s for i, s in enumerate(tensor.shape)] if keepdim else \
+        [s for i, s in enumerate(tensor.shape) if i not in dims]
+    out = DTensor(locals_, tensor.device_mesh, placements, shape)
+    if placements != to_replicate:
+        out = out.redistribute(placements=to_replicate)
+    if kind == "mean":
+        count = math.prod(tensor.shape[d] for d in dims)
+        out = DTensor({g: t / count for g, t in out._locals.items()}, out.device_mesh, out.placements, out.shape)
+    return out

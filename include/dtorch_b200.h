@@ -157,6 +157,14 @@ int dt_all_gather(dt_comm* comm, int rank, const void* in, void* out, size_t out
 int dt_all_to_all(dt_comm* comm, int rank, const void* in, void* out, int ndim, const int64_t* in_shape,
                   int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_bytes, void* stream);
 
+/* Several tensors of one local shape swapped Shard(src_dim) -> Shard(dst_dim) in one launch: ins[t] -> outs[t],
+ * t < ntensors <= 8, each with the layout rules of dt_all_to_all. The q, k and v swaps of Ulysses context
+ * parallelism (python/dtorch/nn/scaled_dot_product_attention_with_cp.py:73-85, three ThreadGroup::AllToAll calls)
+ * become one kernel whose peer stores interleave all three tensors. */
+int dt_all_to_all_multi(dt_comm* comm, int rank, int ntensors, const void* const* ins, void* const* outs, int ndim,
+                        const int64_t* in_shape, int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_bytes,
+                        void* stream);
+
 /* Device-side barrier of all ranks on their streams. Replaces ThreadGroup::Barrier (thread_group.cc:118-125). */
 int dt_barrier(dt_comm* comm, int rank, void* stream);
 

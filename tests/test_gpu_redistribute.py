@@ -174,3 +174,69 @@ def test_ulysses_swap_and_back(mode, n):
     assert torch.equal(z.to_torch(), full)
     for r in range(n):
         assert torch.equal(z.local(r).cpu(), x.local(r).cpu())
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_fused_qkv_all_to_all_matches_separate(mode, n):
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(10 + n)
+    fulls = [torch.randn(2, 8, 40, 16, generator=g).to(torch.bfloat16) for _ in range(3)]  # (N, H, L, E)
+    xs = [dtb.DTensor.from_torch(f, mesh, [dtb.Shard(2)]) for f in fulls]
+    fused = dtb.redistribute_many(xs, [dtb.Shard(1)])
+    torch.cuda.synchronize()
+    for x, y, f in zip(xs, fused, fulls):
+        sep = x.redistribute(placements=[dtb.Shard(1)])
+        torch.cuda.synchronize()
+        for r in range(n):
+            assert torch.equal(y.local(r).cpu(), sep.local(r).cpu())
+        assert torch.equal(y.to_torch(), f)
+
+
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_ulysses_attention_matches_torch(mode, is_causal):
+    n = 4
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,), mesh_dim_names=["cp"])
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(2, 8, 64, 32, generator=g) for _ in range(3))
+    want = torch.nn.functional.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda(), is_causal=is_causal).cpu()
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [dtb.Shard(2)]) for t in (q, k, v))
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, is_causal=is_causal, ulysses_cp_dim="cp")
+    torch.cuda.synchronize()
+    assert out.placements == [dtb.Shard(2)]
+    assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)
+
+
+def test_ring_attention_matches_torch(mode):
+    n = 2
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(4)
+    q, k, v = (torch.randn(1, 4, 48, 16, generator=g) for _ in range(3))
+    want = torch.nn.functional.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [dtb.Shard(2)]) for t in (q, k, v))
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, ring_cp_dim=0)
+    torch.cuda.synchronize()
+    assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("shape,placements,dims", [
+    ((8, 6), ["S0"], [0]),
+    ((9, 7, 4), ["S1"], [1, 2]),
+    ((6, 10), ["S1"], [0]),          # reduce a dim that is not sharded: no communication
+    ((4, 12, 5), ["S2"], [0, 2]),
+])
+def test_reduce_over_sharded_dims(mode, shape, placements, dims):
+    need(mode, 2)
+    mesh = dtb.DeviceMesh("cuda", [0, 1])
+    g = torch.Generator().manual_seed(5)
+    full = torch.randn(*shape, generator=g)
+    x = dtb.DTensor.from_torch(full, mesh, [dtb.Placement(p) for p in placements])
+    for kind in ("sum", "mean"):
+        for keepdim in (False, True):
+            y = dtb.reduce(x, dims, kind=kind, keepdim=keepdim)
+            torch.cuda.synchronize()
+            want = full.sum(dim=dims, keepdim=keepdim) if kind == "sum" else full.mean(dim=dims, keepdim=keepdim)
+            assert tuple(y.shape) == tuple(want.shape)
+            assert torch.allclose(y.to_torch(), want, rtol=1e-5, atol=1e-5), (kind, keepdim)
