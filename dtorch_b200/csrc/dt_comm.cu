@@ -47,7 +47,8 @@ int fail(int status, const std::string& msg) {
         }                                                                                      \
     } while (0)
 
-constexpr size_t kFlagBytes = static_cast<size_t>(kMaxBlocks) * kMaxRanks * sizeof(uint32_t);
+// [kMaxBlocks][kMaxRanks] barrier flags, then kMaxBlocks per-block epoch counters
+constexpr size_t kFlagBytes = static_cast<size_t>(kMaxBlocks) * (kMaxRanks + 1) * sizeof(uint32_t);
 constexpr size_t kHeapOffset = 64 * 1024;  // heap starts 64 KiB into the slab (flags first)
 constexpr uint32_t kHandleMagic = 0x44544232u;  // "DTB2"
 
@@ -93,7 +94,6 @@ struct RankState {
     uint32_t* flags = nullptr;    // this rank's flag array (on dev)
     char* heap = nullptr;
     int* err = nullptr;           // host-mapped error word
-    uint32_t epoch = 0;           // collectives issued by this rank
     uint64_t rv_gen = 0;          // rendezvous generations passed by this rank
     cudaEvent_t ready = nullptr;  // same-device mode
     uint32_t* peer_flags[kMaxRanks] = {};  // flags of rank r as addressed from this rank's device
@@ -201,6 +201,7 @@ int resident_grid(K kernel, int dev, int num_sms) {
 SignalCtx make_sig(dt_comm* c, int rank) {
     SignalCtx s{};
     for (int i = 0; i < kMaxRanks; ++i) s.flags[i] = c->r[rank].peer_flags[i];
+    s.epochs = c->r[rank].flags + kMaxBlocks * kMaxRanks;
     s.err = c->r[rank].err;
     s.rank = rank;
     s.n = c->n;
@@ -1119,10 +1120,7 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
                                c->n >= 6 && bytes >= (static_cast<size_t>(8) << 20);
         if (want_nvls || auto_nvls) {
             NvlsArgs na{};
-            const uint32_t epoch = ++s.epoch;
             na.sig = make_sig(c, rank);
-            na.bar_start = 2 * epoch - 1;
-            na.bar_end = 2 * epoch;
             na.mc_in = s.nvls_mc + nv_in;
             na.mc_out = s.nvls_mc + nv_out;
             const int64_t nvec = static_cast<int64_t>(bytes / 16);
@@ -1142,10 +1140,7 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
     char* outs[kMaxRanks];
     st = resolve_peers(c, rank, in, count * es, out, count * es, ins, outs);
     if (st != DT_OK) return st;
-    const uint32_t epoch = ++s.epoch;
     a.sig = make_sig(c, rank);
-    a.bar_start = 2 * epoch - 1;
-    a.bar_end = 2 * epoch;
     a.n = c->n;
     const int pv = 16 / es;
     bool vec_ok = true;
@@ -1229,10 +1224,7 @@ int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t ou
     st = resolve_peers(c, rank, in, in_count * es, out, out_count * es, ins, outs);
     if (st != DT_OK) return st;
     ReduceArgs a{};
-    const uint32_t epoch = ++s.epoch;
     a.sig = make_sig(c, rank);
-    a.bar_start = 2 * epoch - 1;
-    a.bar_end = 2 * epoch;
     a.n = c->n;
     const int pv = 16 / es;
     // vector path decided from every rank's pointers and the shared chunk size, so all ranks agree
@@ -1298,10 +1290,7 @@ int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer,
     st = resolve_peers(c, rank, in, in_bytes, out, out_bytes, ins, outs);
     if (st != DT_OK) return st;
     CopyArgs<kMaxRanks> a{};
-    const uint32_t epoch = ++s.epoch;
     a.sig = make_sig(c, rank);
-    a.bar_start = 2 * epoch - 1;
-    a.bar_end = 2 * epoch;
     a.nseg = c->n;
     for (int j = 0; j < c->n; ++j) {
         const int k = (rank + 1 + j) % c->n;  // destinations in rotated order, own output last
@@ -1375,10 +1364,7 @@ int dt_all_to_all(dt_comm* c, int rank, const void* in, void* out, int ndim, con
     st = resolve_peers(c, rank, in, in_elems * elem_b, out, out_elems * elem_b, ins, outs);
     if (st != DT_OK) return st;
     CopyArgs<kMaxRanks> a{};
-    const uint32_t epoch = ++s.epoch;
     a.sig = make_sig(c, rank);
-    a.bar_start = 2 * epoch - 1;
-    a.bar_end = 2 * epoch;
     a.nseg = c->n;
     for (int j = 0; j < c->n; ++j) {
         const int k = (rank + 1 + j) % c->n;
@@ -1458,10 +1444,7 @@ int dt_all_to_all_multi(dt_comm* c, int rank, int ntensors, const void* const* i
             for (int r = 0; r < c->n; ++r) outs[t][r] = static_cast<char*>(all[r].extra[t]);
     }
     CopyArgs<kMaxRanks * kMaxRanks> a{};
-    const uint32_t epoch = ++s.epoch;
     a.sig = make_sig(c, rank);
-    a.bar_start = 2 * epoch - 1;
-    a.bar_end = 2 * epoch;
     a.nseg = ntensors * c->n;
     // segment (j * ntensors + t): tensor t to destination (rank + 1 + j) % n -- destinations interleaved
     for (int j = 0; j < c->n; ++j) {
@@ -1490,12 +1473,7 @@ int dt_barrier(dt_comm* c, int rank, void* stream_v) {
     }
     if (c->n == 1) return DT_OK;
     DT_CUDA(cudaSetDevice(s.dev));
-    if (!c->multiprocess) {
-        // peers must have launched up to the same epoch; nothing to exchange but the rendezvous keeps the
-        // host-side generation counters of the ranks in step with the reference's barrier semantics.
-    }
-    const uint32_t epoch = ++s.epoch;
-    k_barrier<<<1, 32, 0, stream>>>(make_sig(c, rank), 2 * epoch - 1, 2 * epoch);
+    k_barrier<<<1, 32, 0, stream>>>(make_sig(c, rank));
     return launch_check("k_barrier");
 }
 

@@ -42,11 +42,26 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // rank). Row b, column s of rank r's array holds the last barrier value block b of rank s announced to r.
 struct SignalCtx {
     uint32_t* flags[kMaxRanks];
-    int* err;  // this rank's error word (host-mapped)
+    uint32_t* epochs;  // this rank's per-block collective counters (local memory, one per block index)
+    int* err;          // this rank's error word (host-mapped)
     int rank;
     int n;
     uint64_t timeout_ns;
 };
+
+// Epoch of this launch for block blockIdx.x: the block's own counter in device memory, advanced once per
+// launch. Every rank launches the same grid for the same collective, so block b has seen the same number of
+// collectives on every rank and agrees with its peers; nothing comes from the host, which keeps a captured
+// CUDA graph correct on replay. Barrier values are 2e-1 (start) and 2e (end).
+__device__ __forceinline__ uint32_t block_epoch(const SignalCtx& s) {
+    __shared__ uint32_t e;
+    if (threadIdx.x == 0) {
+        e = s.epochs[blockIdx.x] + 1;
+        s.epochs[blockIdx.x] = e;
+    }
+    __syncthreads();
+    return e;
+}
 
 // Barrier of block blockIdx.x across all ranks: every prior memory operation of this block (loads of peer
 // inputs, stores into peer outputs) is ordered before the announcement, and nothing after the barrier starts
@@ -183,8 +198,6 @@ struct ReduceArgs {
     int64_t out_shift;    // output element index = input element index - out_shift
     int n;                // number of inputs
     int nout;             // number of outputs
-    uint32_t bar_start;   // barrier values (peer mode)
-    uint32_t bar_end;
 };
 
 template <int DT, int NRMAX, bool STORAGE>
@@ -246,10 +259,14 @@ __device__ __forceinline__ void reduce_scalars(const ReduceArgs& a) {
 
 template <int DT, int NRMAX, bool STORAGE, bool BARRIER>
 __global__ void __launch_bounds__(kThreads) k_reduce(const __grid_constant__ ReduceArgs a) {
-    if (BARRIER && !block_barrier(a.sig, a.bar_start)) return;
+    uint32_t e = 0;
+    if (BARRIER) {
+        e = block_epoch(a.sig);
+        if (!block_barrier(a.sig, 2 * e - 1)) return;
+    }
     reduce_vectors<DT, NRMAX, STORAGE>(a);
     reduce_scalars<DT, STORAGE>(a);
-    if (BARRIER) block_barrier(a.sig, a.bar_end);
+    if (BARRIER) block_barrier(a.sig, 2 * e);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -277,8 +294,6 @@ struct CopyArgs {
     SignalCtx sig;
     int64_t max_items;  // max over segs of items
     int nseg;
-    uint32_t bar_start;
-    uint32_t bar_end;
 };
 
 template <int VW>
@@ -305,7 +320,11 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyA
     using V = typename VecOf<VW>::T;
     constexpr int U = CopyGeom<VW>::kU;
     constexpr int SEG = CopyGeom<VW>::kSegBytes;
-    if (BARRIER && !block_barrier(a.sig, a.bar_start)) return;
+    uint32_t e = 0;
+    if (BARRIER) {
+        e = block_epoch(a.sig);
+        if (!block_barrier(a.sig, 2 * e - 1)) return;
+    }
     const int lane = threadIdx.x & 31;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -347,7 +366,7 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyA
             if (off < len) dst[u * 32 + lane] = buf[u];
         }
     }
-    if (BARRIER) block_barrier(a.sig, a.bar_end);
+    if (BARRIER) block_barrier(a.sig, 2 * e);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -362,8 +381,6 @@ struct NvlsArgs {
     const char* mc_in;  // multicast address of the input
     char* mc_out;       // multicast address of the output
     int64_t vlo, vhi;   // 16-byte vectors handled by this rank
-    uint32_t bar_start;
-    uint32_t bar_end;
 };
 
 template <int DT>
@@ -407,7 +424,8 @@ __device__ __forceinline__ void multimem_st_v4(void* p, const uint4& v) {
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads) k_allreduce_nvls(const __grid_constant__ NvlsArgs a) {
-    if (!block_barrier(a.sig, a.bar_start)) return;
+    const uint32_t e = block_epoch(a.sig);
+    if (!block_barrier(a.sig, 2 * e - 1)) return;
     constexpr int U = 4;
     const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x * U;
     for (int64_t base = a.vlo + static_cast<int64_t>(blockIdx.x) * blockDim.x * U; base < a.vhi; base += step) {
@@ -425,12 +443,13 @@ __global__ void __launch_bounds__(kThreads) k_allreduce_nvls(const __grid_consta
     }
     // the stores went through the multicast alias; peers read the same memory through their unicast mapping
     asm volatile("fence.proxy.alias;" ::: "memory");
-    block_barrier(a.sig, a.bar_end);
+    block_barrier(a.sig, 2 * e);
 }
 
 // Barrier-only kernel (ThreadGroup::Barrier): one block, both phases of the epoch.
-__global__ void k_barrier(const __grid_constant__ SignalCtx s, uint32_t v0, uint32_t v1) {
-    if (block_barrier(s, v0)) block_barrier(s, v1);
+__global__ void k_barrier(const __grid_constant__ SignalCtx s) {
+    const uint32_t e = block_epoch(s);
+    if (block_barrier(s, 2 * e - 1)) block_barrier(s, 2 * e);
 }
 
 }  // namespace dtb

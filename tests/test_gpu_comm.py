@@ -283,3 +283,63 @@ def test_nvls_all_reduce(dtype):
                             capi.DT_ALGO_NVLS | capi.DT_ACCUM_STORAGE, 0)
     finally:
         comm.destroy()
+
+
+def test_peer_collectives_replay_from_cuda_graphs():
+    """Barrier epochs live in device memory, so collectives captured into a CUDA graph stay correct when the
+    graph is replayed: each rank thread captures an all-reduce and an all-to-all, then replays them with new
+    inputs, with eager calls in between."""
+    n = min(ngpu(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    devs = list(range(n))
+    comm = capi.Comm(devs)
+    count = (1 << 20) + 8
+    S, H, D = 16 * n, 2 * n, 32
+    lens = shard_sizes(S, n)
+    try:
+        x = [torch.zeros(count, dtype=torch.bfloat16, device=f"cuda:{r}") for r in devs]
+        y = [torch.zeros_like(t) for t in x]
+        a_in = [torch.zeros(1, lens[r], H, D, dtype=torch.bfloat16, device=f"cuda:{r}") for r in devs]
+        a_out = [torch.zeros(1, S, H // n, D, dtype=torch.bfloat16, device=f"cuda:{r}") for r in devs]
+        streams = [torch.cuda.Stream(device=r) for r in devs]
+        graphs = [torch.cuda.CUDAGraph() for _ in devs]
+
+        def step(r):
+            s = streams[r].cuda_stream
+            comm.all_reduce(r, x[r].data_ptr(), y[r].data_ptr(), count, capi.DT_BFLOAT16, 0, s)
+            comm.all_to_all(r, a_in[r].data_ptr(), a_out[r].data_ptr(), [1, lens[r], H, D], 1, 2, lens, 2, s)
+
+        def capture(r):
+            with torch.cuda.device(r):
+                with torch.cuda.stream(streams[r]):
+                    step(r)  # eager warm-up
+                streams[r].synchronize()
+                with torch.cuda.graph(graphs[r], stream=streams[r], capture_error_mode="thread_local"):
+                    step(r)
+
+        run_ranks(n, capture)
+        g = torch.Generator().manual_seed(9)
+        for it in range(3):
+            host = [torch.randn(count, generator=g).to(torch.bfloat16) for _ in devs]
+            parts = [torch.randn(1, lens[r], H, D, generator=g).to(torch.bfloat16) for r in devs]
+
+            def replay(r):
+                with torch.cuda.device(r), torch.cuda.stream(streams[r]):
+                    x[r].copy_(host[r], non_blocking=False)
+                    a_in[r].copy_(parts[r], non_blocking=False)
+                    graphs[r].replay()
+                    if it == 1:
+                        step(r)  # an eager call between replays advances the same device counters
+                    streams[r].synchronize()
+
+            run_ranks(n, replay)
+            want = R.fold_sum([raw_from_torch(h) for h in host], 1, storage_round=False)
+            full = torch.cat(parts, dim=1)
+            for r in devs:
+                assert np.array_equal(np_raw(y[r]), want), (it, r)
+                assert torch.equal(a_out[r].cpu(), full[:, :, r * (H // n):(r + 1) * (H // n)]), (it, r)
+            assert comm.error(0) == capi.DT_OK
+    finally:
+        del graphs
+        comm.destroy()
