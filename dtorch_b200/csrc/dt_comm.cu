@@ -1115,9 +1115,11 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
         if (want_nvls && storage)
             return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NVLS reduces in the switch with fp32 accumulation; "
                                             "DT_ACCUM_STORAGE is not available with it");
-        // measured at 8 ranks: NVLS ahead of the two-shot kernel from 8-16 MiB up; not measured below 6 ranks
+        // measured: NVLS ahead of the two-shot kernel from 8-16 MiB at 8 ranks and from 16 MiB at 4 ranks;
+        // behind it at 2 ranks (it moves (1+1/n)S per GPU against the two-shot's 2(n-1)/n S)
+        const size_t nvls_min = c->n >= 6 ? (static_cast<size_t>(8) << 20) : (static_cast<size_t>(16) << 20);
         const bool auto_nvls = (flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT | DT_ALGO_NVLS)) == 0 && nvls_ok && !storage &&
-                               c->n >= 6 && bytes >= (static_cast<size_t>(8) << 20);
+                               c->n >= 4 && bytes >= nvls_min;
         if (want_nvls || auto_nvls) {
             NvlsArgs na{};
             na.sig = make_sig(c, rank);
