@@ -469,65 +469,10 @@ def run_reference(args, rank, world):
     print(json.dumps(line))
 
 
-class _CAI:
-    def __init__(self, ptr, numel, typestr):
-        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (numel,), "typestr": typestr, "version": 3,
-                                         "strides": None}
-
-
 def heap_tensor(base, offset, numel, dtype, device):
-    ts = {torch.float32: "<f4", torch.bfloat16: "<i2", torch.float16: "<i2"}[dtype]
-    t = torch.as_tensor(_CAI(base + offset, numel, ts), device=device)
-    return t.view(dtype) if dtype != torch.float32 else t
+    from dtorch_b200.multiprocess import device_view
 
-
-def share_fd(rank, n, fd, tag):
-    """Hand rank 0's file descriptor to every other rank (SCM_RIGHTS over a Unix socket)."""
-    import socket
-
-    import torch.distributed as dist
-
-    path = f"/tmp/dtb_{os.getuid()}_{os.environ.get('MASTER_PORT', '0')}_{tag}.sock"
-    if rank == 0:
-        if os.path.exists(path):
-            os.unlink(path)
-        srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
-        srv.bind(path)
-        srv.listen(n)
-        dist.barrier()
-        for _ in range(n - 1):
-            conn, _ = srv.accept()
-            socket.send_fds(conn, [b"f"], [fd])
-            conn.close()
-        srv.close()
-        os.unlink(path)
-        dist.barrier()
-        return fd
-    dist.barrier()
-    c = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
-    c.connect(path)
-    _, fds, _, _ = socket.recv_fds(c, 16, 1)
-    c.close()
-    dist.barrier()
-    return fds[0]
-
-
-def setup_nvls(comm, rank, n, nbytes):
-    """Bind an NVLS buffer of `nbytes` on every rank of a multi-process communicator; False if unsupported."""
-    import torch.distributed as dist
-
-    ok = torch.tensor([1 if comm.nvls_supported() else 0], device="cuda")
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    if int(ok.item()) == 0:
-        return False
-    fd = comm.nvls_create(nbytes) if rank == 0 else -1
-    fd = share_fd(rank, n, fd, "nvls")
-    comm.nvls_attach(fd, nbytes)
-    dist.barrier()  # every device added before any rank binds memory
-    comm.nvls_bind()
-    dist.barrier()
-    os.close(fd)
-    return True
+    return device_view(base + offset, numel, dtype, device)
 
 
 def run_ours_multi(args, rank, world, local_rank):
@@ -572,10 +517,9 @@ def run_ours_multi(args, rank, world, local_rank):
     align = 1 << 20
     in_bytes = (in_numel * es + align - 1) // align * align
     out_bytes = (out_numel * es + align - 1) // align * align
-    comm = capi.Comm.for_rank(n, rank, local_rank, in_bytes + out_bytes)
-    handles = [None] * n
-    dist.all_gather_object(handles, comm.export_handle())
-    comm.import_handles(handles)
+    from dtorch_b200.multiprocess import create_rank_comm, setup_nvls
+
+    comm = create_rank_comm(in_bytes + out_bytes, local_rank)
     base, _ = comm.heap(rank)
     x = heap_tensor(base, 0, in_numel, dtype, dev)
     y = heap_tensor(base, in_bytes, out_numel, dtype, dev)
@@ -595,7 +539,7 @@ def run_ours_multi(args, rank, world, local_rank):
     ar_flags = 0
     xp, yp = x, y
     if op == "all_reduce" and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
-        if setup_nvls(comm, rank, n, 2 * in_bytes):
+        if setup_nvls(comm, 2 * in_bytes):
             nb, _ = comm.nvls_buffer(rank)
             xn = heap_tensor(nb, 0, in_numel, dtype, dev)
             yn = heap_tensor(nb, in_bytes, out_numel, dtype, dev)
@@ -750,16 +694,15 @@ def run_sweep_multi(args, rank, world, local_rank):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
     max_bytes = 1 << args.sweep_hi
-    comm = capi.Comm.for_rank(n, rank, local_rank, 2 * max_bytes + (4 << 20))
-    handles = [None] * n
-    dist.all_gather_object(handles, comm.export_handle())
-    comm.import_handles(handles)
+    from dtorch_b200.multiprocess import create_rank_comm, setup_nvls
+
+    comm = create_rank_comm(2 * max_bytes + (4 << 20), local_rank)
     base, _ = comm.heap(rank)
     stream = torch.cuda.current_stream(dev)
     ops = args.sweep_ops.split(",")
     nvls_base = 0
     if "all_reduce" in ops and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
-        if setup_nvls(comm, rank, n, 2 * max_bytes + (4 << 20)):
+        if setup_nvls(comm, 2 * max_bytes + (4 << 20)):
             nvls_base, _ = comm.nvls_buffer(rank)
     for op in ops:
         for dtype in ([torch.bfloat16, torch.float32] if op in ("all_reduce", "reduce_scatter") else [torch.bfloat16]):
