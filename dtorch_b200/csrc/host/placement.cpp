@@ -164,8 +164,23 @@ std::map<int64_t, std::vector<int64_t>> ComputeLocalShapes(const std::vector<int
     for (auto id : mesh.ids) out[id] = even;
     for (const auto& kv : infos) {
         const size_t d = static_cast<size_t>(kv.first);
-        if (shape[d] % kv.second.shardSize == 0) continue;
-        const auto split = ShardSizes(shape[d], kv.second.shardSize);
+        // sub-split Shard(d, s) on one mesh dim: piece i = piece i of the first s + 1 rows plus piece i of the
+        // rest (ReplicateToShard, thread_group.cc:339-358; DistributedScather, distributed_scather_and_gather.cc:61-80)
+        int64_t sub = -1;
+        for (auto md : kv.second.meshDims)
+            if (p[md].HasSubSplit()) sub = p[md].subSplit;
+        std::vector<int64_t> split;
+        if (sub >= 0) {
+            if (kv.second.meshDims.size() != 1)
+                throw std::invalid_argument("a sub-split shard dim must be sharded by one mesh dim");
+            if (sub <= 0 || sub >= shape[d]) throw std::invalid_argument("invalid subSplitCoordinates");
+            const auto front = ShardSizes(sub + 1, kv.second.shardSize);
+            const auto back = ShardSizes(shape[d] - sub - 1, kv.second.shardSize);
+            for (size_t i = 0; i < front.size(); ++i) split.push_back(front[i] + back[i]);
+        } else {
+            if (shape[d] % kv.second.shardSize == 0) continue;
+            split = ShardSizes(shape[d], kv.second.shardSize);
+        }
         for (size_t idx = 0; idx < mesh.ids.size(); ++idx) {
             const auto c = Coordinates(mesh, idx);
             int64_t sel = 0;  // row-major index over the selected mesh dims

@@ -22,16 +22,29 @@ from . import _host
 
 
 class Placement:
-    """Replicate ("R"), Partial ("P", pending SUM) or Shard(dim) ("S<dim>")."""
+    """Replicate ("R"), Partial ("P", pending SUM), Shard(dim) ("S<dim>") or the sub-split Shard(dim, s)
+    ("S<dim>/<s>": rank i holds piece i of the first s + 1 rows plus piece i of the rest -- the causal
+    load-balancing layout of the reference's context parallelism)."""
 
     def __init__(self, placement: str):
         self._s = placement
+        self._sub = -1
         if placement in ("R", "P"):
             self._dim = None
         elif placement.startswith("S"):
-            self._dim = int(placement[1:])
+            body = placement[1:]
+            if "/" in body:
+                body, sub = body.split("/")
+                self._sub = int(sub)
+            self._dim = int(body)
         else:
             raise ValueError(f"bad placement {placement!r}")
+
+    def has_sub_split_coordinates(self) -> bool:
+        return self._sub != -1
+
+    def get_sub_split_coordinates(self) -> int:
+        return self._sub
 
     def __eq__(self, other) -> bool:
         return isinstance(other, Placement) and other._s == self._s
@@ -55,8 +68,8 @@ class Placement:
         return self._dim
 
 
-def Shard(dim: int) -> Placement:  # noqa: N802 (reference API name)
-    return Placement(f"S{dim}")
+def Shard(dim: int, sub_split_coordinates: int = -1) -> Placement:  # noqa: N802 (reference API name)
+    return Placement(f"S{dim}" if sub_split_coordinates == -1 else f"S{dim}/{sub_split_coordinates}")
 
 
 def Replicate() -> Placement:  # noqa: N802
@@ -185,6 +198,12 @@ class DTensor:
             p = plc[i]
             if p.is_replicate():
                 parts = [t] * n
+            elif p.is_shard() and p.has_sub_split_coordinates():
+                d, sub = p.get_shard_index(), p.get_sub_split_coordinates()
+                front, back = torch.split(t, [sub + 1, t.shape[d] - sub - 1], d)
+                fronts = torch.split(front, _host.shard_sizes(sub + 1, n), d)
+                backs = torch.split(back, _host.shard_sizes(t.shape[d] - sub - 1, n), d)
+                parts = [torch.cat([fronts[k], backs[k]], d) for k in range(n)]
             elif p.is_shard():
                 d = p.get_shard_index()
                 parts = list(torch.split(t, _host.shard_sizes(t.shape[d], n), d))
@@ -206,6 +225,12 @@ class DTensor:
             if p.is_replicate():
                 return gather(m[0], i + 1)
             parts = [gather(m[k], i + 1) for k in range(m.shape[0])]
+            if p.is_shard() and p.has_sub_split_coordinates():
+                d, sub = p.get_shard_index(), p.get_sub_split_coordinates()
+                fs = _host.shard_sizes(sub + 1, len(parts))
+                fronts = [x.narrow(d, 0, fs[k]) for k, x in enumerate(parts)]
+                backs = [x.narrow(d, fs[k], x.shape[d] - fs[k]) for k, x in enumerate(parts)]
+                return torch.cat([torch.cat(fronts, d), torch.cat(backs, d)], d)
             if p.is_shard():
                 return torch.cat(parts, p.get_shard_index())
             acc = parts[0]

@@ -343,3 +343,111 @@ def test_peer_collectives_replay_from_cuda_graphs():
     finally:
         del graphs
         comm.destroy()
+
+
+def _peer_or_skip(n):
+    if ngpu() < n:
+        pytest.skip(f"needs {n} GPUs")
+    return list(range(n))
+
+
+@pytest.mark.parametrize("dim", [0, 1, 2])
+@pytest.mark.parametrize("inner", [4, 3, 1])  # 3 and 1 bf16 elements give odd byte runs (narrow vector paths)
+def test_peer_all_gather_layouts(dim, inner):
+    n = min(ngpu(), 4)
+    devs = _peer_or_skip(max(n, 2))
+    n = len(devs)
+    full = [7, 5 * n + 3, inner]
+    lens = shard_sizes(full[dim], n)
+    g = torch.Generator().manual_seed(dim * 10 + inner)
+    parts = []
+    for r in range(n):
+        shp = list(full)
+        shp[dim] = lens[r]
+        parts.append(torch.randn(*shp, generator=g).to(torch.bfloat16))
+    comm = capi.Comm(devs)
+    try:
+        outs = [None] * n
+        outer = int(np.prod(full[:dim]))
+        inner_b = int(np.prod(full[dim + 1:])) * 2
+
+        def fn(r):
+            with torch.cuda.device(r):
+                x = parts[r].to(f"cuda:{r}")
+                o = torch.empty(outer * sum(lens) * inner_b // 2, dtype=torch.bfloat16, device=f"cuda:{r}")
+                comm.all_gather(r, x.data_ptr(), o.data_ptr(), outer, lens, inner_b, torch.cuda.current_stream(r).cuda_stream)
+                torch.cuda.current_stream(r).synchronize()
+                outs[r] = o
+
+        run_ranks(n, fn)
+        want = R.all_gather([raw_from_torch(p) for p in parts], dim)
+        for r in range(n):
+            assert np.array_equal(np_raw(outs[r]).reshape(want.shape), want), r
+    finally:
+        comm.destroy()
+
+
+@pytest.mark.parametrize("src_dim,dst_dim", [(1, 2), (2, 1), (0, 3), (3, 0)])
+@pytest.mark.parametrize("last", [16, 3])
+def test_peer_all_to_all_layouts(src_dim, dst_dim, last):
+    n = min(ngpu(), 4)
+    devs = _peer_or_skip(max(n, 2))
+    n = len(devs)
+    full = [2 * n + 1, 3 * n + 2, 2 * n + 3, last * n + 1]
+    src_lens = shard_sizes(full[src_dim], n)
+    g = torch.Generator().manual_seed(src_dim * 7 + dst_dim + last)
+    parts = []
+    for r in range(n):
+        shp = list(full)
+        shp[src_dim] = src_lens[r]
+        parts.append(torch.randn(*shp, generator=g))
+    split = shard_sizes(full[dst_dim], n)
+    comm = capi.Comm(devs)
+    try:
+        outs = [None] * n
+
+        def fn(r):
+            with torch.cuda.device(r):
+                x = parts[r].to(f"cuda:{r}")
+                oshape = list(full)
+                oshape[dst_dim] = split[r]
+                o = torch.empty(oshape, device=f"cuda:{r}")
+                comm.all_to_all(r, x.data_ptr(), o.data_ptr(), list(parts[r].shape), src_dim, dst_dim, src_lens, 4,
+                                torch.cuda.current_stream(r).cuda_stream)
+                torch.cuda.current_stream(r).synchronize()
+                outs[r] = o
+
+        run_ranks(n, fn)
+        want = R.all_to_all([p.numpy() for p in parts], src_dim, dst_dim)
+        for r in range(n):
+            assert np.array_equal(outs[r].cpu().numpy(), want[r]), r
+    finally:
+        comm.destroy()
+
+
+@pytest.mark.parametrize("out_count", [1, 13, 4096 + 5, (1 << 18) + 7])
+def test_peer_reduce_scatter_fp16_odd_chunks(out_count):
+    n = min(ngpu(), 8)
+    devs = _peer_or_skip(max(n, 2))
+    n = len(devs)
+    g = torch.Generator().manual_seed(out_count)
+    parts = [torch.randn(n * out_count, generator=g).to(torch.float16) for _ in range(n)]
+    comm = capi.Comm(devs)
+    try:
+        outs = [None] * n
+
+        def fn(r):
+            with torch.cuda.device(r):
+                x = parts[r].to(f"cuda:{r}")
+                o = torch.empty(out_count, dtype=torch.float16, device=f"cuda:{r}")
+                comm.reduce_scatter(r, x.data_ptr(), o.data_ptr(), out_count, capi.DT_FLOAT16, 0,
+                                    torch.cuda.current_stream(r).cuda_stream)
+                torch.cuda.current_stream(r).synchronize()
+                outs[r] = o
+
+        run_ranks(n, fn)
+        want = R.reduce_scatter([raw_from_torch(p) for p in parts], 2, storage_round=False)
+        for r in range(n):
+            assert np.array_equal(np_raw(outs[r]), want[r]), r
+    finally:
+        comm.destroy()

@@ -240,3 +240,22 @@ def test_reduce_over_sharded_dims(mode, shape, placements, dims):
             want = full.sum(dim=dims, keepdim=keepdim) if kind == "sum" else full.mean(dim=dims, keepdim=keepdim)
             assert tuple(y.shape) == tuple(want.shape)
             assert torch.allclose(y.to_torch(), want, rtol=1e-5, atol=1e-5), (kind, keepdim)
+
+
+@pytest.mark.parametrize("n,length,sub", [(2, 6, 2), (2, 9, 4), (4, 16, 7), (4, 19, 5)])
+def test_sub_split_shard_round_trip(mode, n, length, sub):
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(length + sub)
+    full = torch.randn(3, length, 5, generator=g)
+    ss = dtb.Shard(1, sub)
+    x = dtb.DTensor.from_torch(full, mesh, [ss])
+    assert torch.equal(x.to_torch(), full)
+    r = x.redistribute(placements=[dtb.Replicate()])  # all-gather into pieces + sub-split reassembly
+    torch.cuda.synchronize()
+    for gid in range(n):
+        assert torch.equal(r.local(gid).cpu(), full)
+    back = r.redistribute(placements=[ss])  # local sub-split slicing
+    torch.cuda.synchronize()
+    for gid in range(n):
+        assert torch.equal(back.local(gid).cpu(), x.local(gid).cpu())

@@ -62,3 +62,10 @@ def test_check_valid_rejects(shape, mesh, ids, pl):
 def test_check_valid_accepts():
     h.check_valid([5, 9], [2], [0, 1], ["S1"])
     h.check_valid([2, 16, 128, 128], [2, 2, 2], list(range(8)), ["S0", "S2", "S2"])
+
+
+def test_sub_split_local_shapes():
+    # piece i = shard-rule piece of the first s + 1 rows + shard-rule piece of the rest
+    assert h.compute_local_shapes([6, 4], [2], [0, 1], ["S0/2"]) == {0: [4, 4], 1: [2, 4]}
+    assert h.compute_local_shapes([9, 4], [2], [0, 1], ["S0/4"]) == {0: [5, 4], 1: [4, 4]}
+    assert h.compute_local_shapes([2, 16, 3], [4], [0, 1, 2, 3], ["S1/7"]) == {i: [2, 4, 3] for i in range(4)}
