@@ -246,13 +246,27 @@ class DTensor:
         """Tensor.redistribute (python/dtorch/tensor.py:299-309): same mesh, new placements."""
         assert device_mesh is not None or placements is not None
         device_mesh = device_mesh if device_mesh is not None else self.device_mesh
-        if device_mesh != self.device_mesh:
-            raise NotImplementedError("moving a DTensor between device meshes is not part of this library yet")
         placements = list(placements) if placements is not None else list(self.placements)
+        if device_mesh != self.device_mesh:
+            # placements first on the current mesh, then the move (ConvertKernel::ConvertDeviceMesh,
+            # convert_kernel.cc:79-102: rank i of the source mesh hands its local tensor to rank i of the
+            # destination mesh)
+            here = self.redistribute(placements=placements) if placements != self.placements else self
+            return here._move_to_mesh(device_mesh)
         new = _host.redistribute(self._locals, list(device_mesh.shape), device_mesh.ids, _strings(self.placements),
                                  _strings(placements), list(self.shape))
         normalized = _host.normalize(_strings(placements), list(device_mesh.shape), device_mesh.ids, len(self.shape))
         return DTensor(new, device_mesh, [Placement(p) for p in normalized], self.shape)
+
+    def _move_to_mesh(self, mesh: DeviceMesh) -> "DTensor":
+        if tuple(mesh.shape) != tuple(self.device_mesh.shape):
+            raise ValueError(f"device meshes differ in shape: {self.device_mesh.shape} vs {mesh.shape}")
+        out = {}
+        for src, dst in zip(self.device_mesh.ids, mesh.ids):
+            t = self._locals[src]
+            # a peer copy over NVLink between the two GPUs, ordered on both devices' current streams
+            out[dst] = t.to(f"cuda:{cuda_device_of(dst)}", non_blocking=True)
+        return DTensor(out, mesh, self.placements, self.shape)
 
     def redistribute_like(self, other: "DTensor") -> "DTensor":
         return self.redistribute(device_mesh=other.device_mesh, placements=other.placements)

@@ -259,3 +259,21 @@ def test_sub_split_shard_round_trip(mode, n, length, sub):
     torch.cuda.synchronize()
     for gid in range(n):
         assert torch.equal(back.local(gid).cpu(), x.local(gid).cpu())
+
+
+def test_redistribute_to_another_mesh(mode):
+    # pipeline-stage handoff: mesh [0, 1] -> mesh [2, 3] (peer mode needs 4 GPUs), optionally changing placements
+    need(mode, 4)
+    a = dtb.DeviceMesh("cuda", [0, 1])
+    b = dtb.DeviceMesh("cuda", [2, 3])
+    g = torch.Generator().manual_seed(8)
+    full = torch.randn(6, 10, generator=g)
+    x = dtb.DTensor.from_torch(full, a, [dtb.Shard(0)])
+    y = x.redistribute(device_mesh=b)
+    z = x.redistribute(device_mesh=b, placements=[dtb.Shard(1)])
+    torch.cuda.synchronize()
+    assert y.device_mesh == b and y.placements == [dtb.Shard(0)]
+    assert torch.equal(y.to_torch(), full) and torch.equal(z.to_torch(), full)
+    assert z.placements == [dtb.Shard(1)]
+    for dst in (2, 3):
+        assert y.local(dst).device.index == dtb.cuda_device_of(dst)
