@@ -7,7 +7,13 @@ Layout (N, H, L, E); q, k and v are sharded on the sequence (Shard(2)) along the
   launch per device (the reference issues three redistributes), each device runs attention for its heads over
   the whole sequence, and the output returns to Shard(2).
 * "Ring" (as the reference implements it): K and V are all-gathered along the ring dim (Shard(2) ->
-  Replicate) and each device attends its query chunk to the whole key/value sequence (non-causal only here).
+  Replicate) and each device attends its query chunk to the whole key/value sequence.
+
+Without a causal mask the order of the sequence does not matter, so sub-split sequence shards are viewed as
+plain Shard(2) for the call and the output is viewed back (scaled_dot_product_attention_with_cp.py:44-62,
+:111-112). With `is_causal` each device calls torch's attention on its local query chunk with `is_causal=True`,
+as the reference's SdpaOp::Compute does (scaled_dot_product_attention_op.cc:104-109): for a local query chunk
+shorter than the gathered key sequence that is torch's top-left aligned mask.
 """
 
 from __future__ import annotations
@@ -38,11 +44,14 @@ def scaled_dot_product_attention_with_cp(query: DTensor, key: DTensor, value: DT
     r = _dim_index(query, ring_cp_dim)
     if key.placements != query.placements or value.placements != query.placements:
         raise RuntimeError("query, key and value have different placements")
+    old_placements = list(query.placements)
+    if not is_causal:
+        plain = [Shard(p.get_shard_index()) if p.is_shard() and p.has_sub_split_coordinates() else p
+                 for p in old_placements]
+        query, key, value = query.view(plain), key.view(plain), value.view(plain)
     for d in (u, r):
         if d is not None and query.placements[d] != Shard(2):
             raise ValueError("context-parallel dims must shard the sequence dim (Shard(2))")
-    if r is not None and is_causal:
-        raise NotImplementedError("causal attention with an all-gathered (ring) K/V needs the sub-split layout")
     mesh = query.device_mesh
     placements = list(query.placements)
     if u is not None:
@@ -70,5 +79,5 @@ def scaled_dot_product_attention_with_cp(query: DTensor, key: DTensor, value: DT
     out_shape = tuple(query.shape[:3]) + (value.shape[3],)
     out = DTensor(out_locals, mesh, query.placements, out_shape)
     if u is not None:
-        return out.redistribute(placements=placements)
-    return out
+        out = out.redistribute(placements=placements)
+    return out if is_causal else out.view(old_placements)

@@ -271,6 +271,21 @@ class DTensor:
     def redistribute_like(self, other: "DTensor") -> "DTensor":
         return self.redistribute(device_mesh=other.device_mesh, placements=other.placements)
 
+    def view(self, placements: Sequence[Placement]) -> "DTensor":
+        """Tensor.view(placements) (python/dtorch/tensor.py:439-447): the same local tensors read under other
+        placements, no data movement (e.g. Shard(2, s) viewed as Shard(2) when the order of the sequence does
+        not matter). Every device's local shape must stay the same."""
+        mesh = self.device_mesh
+        placements = [Placement(p) for p in _host.normalize(_strings(placements), list(mesh.shape), mesh.ids,
+                                                            len(self.shape))]
+        _host.check_valid(list(self.shape), list(mesh.shape), mesh.ids, _strings(placements))
+        shapes = _host.compute_local_shapes(list(self.shape), list(mesh.shape), mesh.ids, _strings(placements))
+        for gid, t in self._locals.items():
+            if list(t.shape) != list(shapes[gid]):
+                raise ValueError(f"view {placements} changes device {gid}'s local shape {tuple(t.shape)} to "
+                                 f"{tuple(shapes[gid])}")
+        return DTensor(self._locals, mesh, placements, self.shape)
+
     def __repr__(self) -> str:
         return f"DTensor(shape={self.shape}, mesh={self.device_mesh}, placements={self.placements})"
 

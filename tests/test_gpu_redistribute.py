@@ -277,3 +277,38 @@ def test_redistribute_to_another_mesh(mode):
     assert z.placements == [dtb.Shard(1)]
     for dst in (2, 3):
         assert y.local(dst).device.index == dtb.cuda_device_of(dst)
+
+
+def test_ring_attention_causal_as_reference(mode):
+    # the reference runs torch's attention per device on its query chunk against the gathered K/V with
+    # is_causal=True (SdpaOp::Compute): the result is that, chunk by chunk
+    n = 2
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(6)
+    q, k, v = (torch.randn(1, 4, 48, 16, generator=g) for _ in range(3))
+    chunks = torch.split(q, dtb.dtensor._host.shard_sizes(48, n), 2)
+    want = torch.cat([torch.nn.functional.scaled_dot_product_attention(c.cuda(), k.cuda(), v.cuda(),
+                                                                       is_causal=True).cpu() for c in chunks], 2)
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [dtb.Shard(2)]) for t in (q, k, v))
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, is_causal=True, ring_cp_dim=0)
+    torch.cuda.synchronize()
+    assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("cp", ["ring", "ulysses"])
+def test_attention_on_sub_split_sequence(mode, cp):
+    # non-causal: sub-split sequence shards are viewed as Shard(2) for the call and the output viewed back
+    n = 2
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,), mesh_dim_names=["cp"])
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(1, 4, 40, 16, generator=g) for _ in range(3))
+    want = torch.nn.functional.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    ss = dtb.Shard(2, 13)
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [ss]) for t in (q, k, v))
+    kw = {"ring_cp_dim": "cp"} if cp == "ring" else {"ulysses_cp_dim": "cp"}
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, **kw)
+    torch.cuda.synchronize()
+    assert out.placements == [ss]
+    assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)

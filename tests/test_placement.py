@@ -69,3 +69,18 @@ def test_sub_split_local_shapes():
     assert h.compute_local_shapes([6, 4], [2], [0, 1], ["S0/2"]) == {0: [4, 4], 1: [2, 4]}
     assert h.compute_local_shapes([9, 4], [2], [0, 1], ["S0/4"]) == {0: [5, 4], 1: [4, 4]}
     assert h.compute_local_shapes([2, 16, 3], [4], [0, 1, 2, 3], ["S1/7"]) == {i: [2, 4, 3] for i in range(4)}
+
+
+def test_view_keeps_locals_and_checks_local_shapes():
+    # Tensor.view(placements): metadata only; sub-split Shard(1, 4) of length 9 on 2 devices has local lengths
+    # 5 and 4 (front 3+2, back 2+2), the same as Shard(1), so the view is allowed; Shard(0) is not
+    torch = pytest.importorskip("torch")
+    import dtorch_b200 as dtb
+    mesh = dtb.DeviceMesh("cuda", [0, 1])
+    locs = {0: torch.zeros(3, 5, 2), 1: torch.ones(3, 4, 2)}
+    x = dtb.DTensor(locs, mesh, [dtb.Shard(1, 4)], (3, 9, 2))
+    y = x.view([dtb.Shard(1)])
+    assert y.placements == [dtb.Shard(1)] and y.local(1) is locs[1]
+    assert y.view([dtb.Shard(1, 4)]).placements == [dtb.Shard(1, 4)]
+    with pytest.raises(ValueError):
+        x.view([dtb.Shard(0)])
