@@ -25,7 +25,7 @@ def test_multiprocess_collectives_match_oracle():
     ngpu = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if ngpu < 2:
         pytest.skip("needs >= 2 GPUs")
-    n = min(ngpu, 4)
+    n = min(ngpu, 8)
     env = dict(os.environ, DTORCH_COMM_TIMEOUT_SECOND="30")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}", "--master-addr",
            "127.0.0.1", "--master-port", str(_free_port()), os.path.join(ROOT, "tests", "mp_parity_worker.py")]
