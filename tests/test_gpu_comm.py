@@ -223,8 +223,8 @@ def test_same_device_rendezvous_times_out_cleanly():
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_nvls_all_reduce(dtype):
     """NVLS all-reduce (reduction inside the NVSwitch): within the north-star tolerance of the rank-order
-    fold, identical on every rank and from run to run; in place; picked by default for NVLS buffers at
-    >= 4 ranks and >= 1 MiB."""
+    fold, identical on every rank and from run to run; in place. The default algorithm on NVLS buffers is the
+    rank-order kernel below the switch-over size (16 MiB at 4-5 ranks, 8 MiB at 6+) and NVLS from there."""
     n = min(ngpu(), 8)
     if n < 2:
         pytest.skip("needs >= 2 GPUs")
@@ -269,18 +269,55 @@ def test_nvls_all_reduce(dtype):
             assert np.array_equal(first[r], first[0]), "ranks disagree"
             assert_close(first[r], want, name)
         assert comm.error(0) == capi.DT_OK
-        if n >= 4:  # default algorithm on NVLS buffers
-            for y in ys:
-                y.zero_()
-            torch.cuda.synchronize()
-            run(0)
-            assert np.array_equal(np_raw(ys[0]), first[0])
+        for y in ys:  # default algorithm on NVLS buffers below the switch-over size: the rank-order fold
+            y.zero_()
+        torch.cuda.synchronize()
+        run(0)
+        for r in range(n):
+            assert np.array_equal(np_raw(ys[r]), want)
         run(capi.DT_ALGO_NVLS, in_place=True)
         for r in range(n):
             assert np.array_equal(np_raw(xs[r]), first[0])
         with pytest.raises(capi.DtError):  # storage rounding is not available in the switch
             comm.all_reduce(0, xs[0].data_ptr(), ys[0].data_ptr(), count, code,
                             capi.DT_ALGO_NVLS | capi.DT_ACCUM_STORAGE, 0)
+    finally:
+        comm.destroy()
+
+
+def test_nvls_picked_by_default_from_switch_over_size():
+    n = min(ngpu(), 8)
+    if n < 4:
+        pytest.skip("NVLS is the default from 4 ranks")
+    comm = capi.Comm(list(range(n)))
+    try:
+        if not comm.nvls_supported():
+            pytest.skip("NVLink multicast not supported here")
+        count = ((8 if n >= 6 else 16) << 20) // 2 + 64  # bf16, just above the switch-over size
+        comm.nvls_alloc(2 * count * 2 + (1 << 20))
+        g = torch.Generator().manual_seed(9)
+        host = [torch.randn(count, generator=g).to(torch.bfloat16) for _ in range(n)]
+        xs, ys = [], []
+        for r in range(n):
+            base, _ = comm.nvls_buffer(r)
+            xs.append(view_device_memory(base, count, torch.bfloat16, r))
+            ys.append(view_device_memory(base + count * 2 + 4096, count, torch.bfloat16, r))
+            xs[r].copy_(host[r].to(f"cuda:{r}"))
+        torch.cuda.synchronize()
+        outs = {}
+        for flags in (capi.DT_ALGO_NVLS, 0):
+            def fn(r):
+                with torch.cuda.device(r):
+                    s = torch.cuda.current_stream(r)
+                    comm.all_reduce(r, xs[r].data_ptr(), ys[r].data_ptr(), count, capi.DT_BFLOAT16, flags,
+                                    s.cuda_stream)
+                    s.synchronize()
+            run_ranks(n, fn)
+            outs[flags] = [np_raw(y) for y in ys]
+        want = R.fold_sum([raw_from_torch(h) for h in host], DT_CODE["bfloat16"], storage_round=False)
+        for r in range(n):
+            assert np.array_equal(outs[0][r], outs[capi.DT_ALGO_NVLS][r])
+            assert_close(outs[0][r], want, "bfloat16")
     finally:
         comm.destroy()
 
