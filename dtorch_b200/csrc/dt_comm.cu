@@ -1152,7 +1152,10 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
     }
     int algo = flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT);
     if (algo == 0) algo = (count * es <= static_cast<size_t>(256) * 1024) ? DT_ALGO_ONESHOT : DT_ALGO_TWOSHOT;
-    if (in == out) algo = DT_ALGO_TWOSHOT;  // one-shot would overwrite inputs peers still read
+    // one-shot would overwrite an input that peers still read; decided from every rank's pointers so that all
+    // ranks pick the same kernel even when only some of them reduce in place
+    for (int r = 0; r < c->n; ++r)
+        if (ins[r] == outs[r]) algo = DT_ALGO_TWOSHOT;
     if (algo == DT_ALGO_ONESHOT) {
         a.out[0] = outs[rank];
         a.nout = 1;

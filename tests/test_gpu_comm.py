@@ -175,6 +175,38 @@ def test_peer_in_place_all_reduce_and_heap_buffers():
         comm.destroy()
 
 
+@pytest.mark.parametrize("count", [1000, 64 * 1024 + 3])
+def test_peer_all_reduce_some_ranks_in_place(count):
+    """Even ranks reduce in place, odd ranks into a separate output: every rank still takes the same kernel
+    (the algorithm is chosen from all ranks' pointers), and all get the rank-order sum."""
+    n = min(ngpu(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    comm = capi.Comm(list(range(n)))
+    try:
+        g = torch.Generator().manual_seed(count)
+        host = [torch.randn(count, generator=g) for _ in range(n)]
+        xs = [host[r].to(f"cuda:{r}") for r in range(n)]
+        ys = [xs[r] if r % 2 == 0 else torch.empty_like(xs[r]) for r in range(n)]
+        torch.cuda.synchronize()
+
+        def fn(r):
+            with torch.cuda.device(r):
+                s = torch.cuda.current_stream(r)
+                comm.all_reduce(r, xs[r].data_ptr(), ys[r].data_ptr(), count, capi.DT_FLOAT32, 0, s.cuda_stream)
+                s.synchronize()
+
+        run_ranks(n, fn)
+        want = R.fold_sum([h.numpy() for h in host], 0, storage_round=False)
+        for r in range(n):
+            assert np.array_equal(ys[r].cpu().numpy(), want), r
+        for r in range(1, n, 2):
+            assert torch.equal(xs[r].cpu(), host[r])  # out-of-place ranks keep their input
+        assert comm.error(0) == capi.DT_OK
+    finally:
+        comm.destroy()
+
+
 def test_peer_device_wait_times_out_cleanly():
     """Rank 1 never launches: rank 0's barrier kernel gives up after the 1 s limit, records DT_ERR_TIMEOUT
     in the host-mapped error word and returns; the context stays usable."""
