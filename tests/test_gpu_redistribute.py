@@ -312,3 +312,49 @@ def test_attention_on_sub_split_sequence(mode, cp):
     torch.cuda.synchronize()
     assert out.placements == [ss]
     assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,S", [(2, 45), (4, 64)])
+def test_ring_attention_overlapped_matches_torch(mode, n, S):
+    # own-chunk attention during the K/V all-gather, other chunks after, merged by log-sum-exp
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,), mesh_dim_names=["ring"])
+    g = torch.Generator().manual_seed(S)
+    q, k, v = (torch.randn(2, 4, S, 16, generator=g) for _ in range(3))
+    want = torch.nn.functional.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [dtb.Shard(2)]) for t in (q, k, v))
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, ring_cp_dim="ring", ring_overlap=True)
+    torch.cuda.synchronize()
+    assert out.placements == [dtb.Shard(2)]
+    assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)
+
+
+def test_ring_attention_overlapped_bf16(mode):
+    n = 2
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,))
+    g = torch.Generator().manual_seed(12)
+    q, k, v = (torch.randn(1, 8, 96, 64, generator=g).to(torch.bfloat16) for _ in range(3))
+    want = torch.nn.functional.scaled_dot_product_attention(q.float().cuda(), k.float().cuda(), v.float().cuda()).cpu()
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [dtb.Shard(2)]) for t in (q, k, v))
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, ring_cp_dim=0, ring_overlap=True)
+    torch.cuda.synchronize()
+    got = out.to_torch().float()
+    assert got.dtype == torch.float32 and out.dtype == torch.bfloat16
+    assert torch.allclose(got, want, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_ulysses_and_ring_attention_on_2d_mesh(mode, overlap):
+    need(mode, 4)
+    mesh = dtb.init_device_mesh("cuda", (2, 2), mesh_dim_names=["u", "r"])
+    g = torch.Generator().manual_seed(14)
+    q, k, v = (torch.randn(1, 4, 48, 16, generator=g) for _ in range(3))
+    want = torch.nn.functional.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    pl = [dtb.Shard(2), dtb.Shard(2)]
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, pl) for t in (q, k, v))
+    out = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, ulysses_cp_dim="u", ring_cp_dim="r",
+                                                   ring_overlap=overlap)
+    torch.cuda.synchronize()
+    assert out.placements == pl
+    assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)

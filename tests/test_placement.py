@@ -84,3 +84,13 @@ def test_view_keeps_locals_and_checks_local_shapes():
     assert y.view([dtb.Shard(1, 4)]).placements == [dtb.Shard(1, 4)]
     with pytest.raises(ValueError):
         x.view([dtb.Shard(0)])
+
+
+def test_ring_overlap_argument_checks():
+    torch = pytest.importorskip("torch")
+    import dtorch_b200 as dtb
+    mesh = dtb.DeviceMesh("cuda", [0, 1], mesh_dim_names=["ring"])
+    t = dtb.DTensor({0: torch.zeros(1, 2, 4, 8), 1: torch.zeros(1, 2, 4, 8)}, mesh, [dtb.Shard(2)], (1, 2, 8, 8))
+    for kw in ({"is_causal": True, "ring_cp_dim": "ring"}, {"dropout_p": 0.1, "ring_cp_dim": "ring"}, {}):
+        with pytest.raises(ValueError):
+            dtb.scaled_dot_product_attention_with_cp(t, t, t, ring_overlap=True, **kw)
