@@ -44,11 +44,13 @@ def _dim_index(tensor: DTensor, dim: Optional[Union[int, str]]) -> Optional[int]
 def _attend_with_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float]):
     """Attention of q to one key/value chunk, and the log-sum-exp of each query row's scaled scores
     (fp32, (N, H, L))."""
-    if q.dtype in (torch.float16, torch.bfloat16) and q.shape[-1] % 8 == 0 and q.shape[-1] <= 256:
-        out, lse = torch.ops.aten._scaled_dot_product_flash_attention(q, k, v, 0.0, False, False, scale=scale)[:2]
-    else:  # the memory-efficient kernel (its log-sum-exp rows are padded to a multiple of 32)
-        out, lse = torch.ops.aten._scaled_dot_product_efficient_attention(q, k, v, None, True, 0.0, False,
-                                                                          scale=scale)[:2]
+    if q.dtype in (torch.float16, torch.bfloat16) and q.shape[-1] % 8 == 0 and q.shape[-1] <= 128:
+        # cuDNN's fused attention: the kernel torch's own dispatch picks for these inputs on B200
+        out, lse = torch.ops.aten._scaled_dot_product_cudnn_attention(q, k, v, None, True, 0.0, False, False,
+                                                                      scale=scale)[:2]
+        return out, lse.reshape(lse.shape[:3])
+    # the memory-efficient kernel (its log-sum-exp rows are padded to a multiple of 32)
+    out, lse = torch.ops.aten._scaled_dot_product_efficient_attention(q, k, v, None, True, 0.0, False, scale=scale)[:2]
     return out, lse[..., : q.shape[2]]
 
 
