@@ -94,3 +94,52 @@ def test_ring_overlap_argument_checks():
     for kw in ({"is_causal": True, "ring_cp_dim": "ring"}, {"dropout_p": 0.1, "ring_cp_dim": "ring"}, {}):
         with pytest.raises(ValueError):
             dtb.scaled_dot_product_attention_with_cp(t, t, t, ring_overlap=True, **kw)
+
+
+def _local_shapes_restated(shape, mesh_shape, ids, placements):
+    """DistributedSpec::ComputeLocalShape (dtorch/api/cpp/distributed_spec.cc:539-587) in plain Python: a tensor dim
+    sharded by several mesh dims is split by the product of their sizes, row-major over those mesh dims, with the
+    shard rule (the first L % k pieces one longer)."""
+    import itertools
+    info = {}
+    for md, p in enumerate(placements):
+        if p.startswith("S"):
+            info.setdefault(int(p[1:]), []).append(md)
+    out = {}
+    for idx, coord in enumerate(itertools.product(*[range(m) for m in mesh_shape])):
+        local = list(shape)
+        for d, mds in info.items():
+            k, sel = 1, 0
+            for md in mds:
+                k *= mesh_shape[md]
+                sel = sel * mesh_shape[md] + coord[md]
+            local[d] = shape[d] // k + (1 if sel < shape[d] % k else 0)
+        out[ids[idx]] = local
+    return out
+
+
+def test_local_shapes_match_restatement_on_random_meshes():
+    hyp = pytest.importorskip("hypothesis")
+    st = pytest.importorskip("hypothesis.strategies")
+
+    @hyp.settings(max_examples=300, deadline=None)
+    @hyp.given(st.data())
+    def check(data):
+        mesh_shape = data.draw(st.lists(st.integers(2, 4), min_size=1, max_size=3))
+        ndim = data.draw(st.integers(1, 4))
+        placements = data.draw(st.lists(st.sampled_from(["R", "P"] + [f"S{d}" for d in range(ndim)]),
+                                        min_size=len(mesh_shape), max_size=len(mesh_shape)))
+        ways = {}
+        for md, p in enumerate(placements):
+            if p.startswith("S"):
+                ways[int(p[1:])] = ways.get(int(p[1:]), 1) * mesh_shape[md]
+        shape = [data.draw(st.integers(ways.get(d, 1), 3 * ways.get(d, 1) + 5)) for d in range(ndim)]
+        count = 1
+        for m in mesh_shape:
+            count *= m
+        ids = data.draw(st.permutations(list(range(count))))
+        h.check_valid(shape, mesh_shape, ids, placements)
+        got = h.compute_local_shapes(shape, mesh_shape, ids, placements)
+        assert got == _local_shapes_restated(shape, mesh_shape, ids, placements)
+
+    check()
