@@ -17,13 +17,18 @@ import torch.distributed as dist
 from . import capi
 
 
+def exchange_handles(comm) -> None:
+    """Give every rank every rank's exported communicator handle, in rank order, and import them."""
+    handles = [None] * dist.get_world_size()
+    dist.all_gather_object(handles, comm.export_handle())
+    comm.import_handles(handles)
+
+
 def create_rank_comm(heap_bytes: int, local_device: int) -> capi.Comm:
     """This process's rank of a communicator spanning the default process group, peers mapped."""
     rank, n = dist.get_rank(), dist.get_world_size()
     comm = capi.Comm.for_rank(n, rank, local_device, heap_bytes)
-    handles = [None] * n
-    dist.all_gather_object(handles, comm.export_handle())
-    comm.import_handles(handles)
+    exchange_handles(comm)
     return comm
 
 
@@ -59,7 +64,7 @@ def share_fd(fd: int, tag: str) -> int:
 def setup_nvls(comm: capi.Comm, nbytes: int) -> bool:
     """Bind an NVLS buffer of `nbytes` on every rank (create -> hand the fd over -> attach -> barrier -> bind).
     Returns False, with nothing allocated, when any rank's device lacks NVLink multicast."""
-    ok = torch.tensor([1 if comm.nvls_supported() else 0], device="cuda")
+    ok = torch.tensor([1 if comm.nvls_supported() else 0], device="cuda" if dist.get_backend() == "nccl" else "cpu")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if int(ok.item()) == 0:
         return False
