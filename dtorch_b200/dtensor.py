@@ -111,6 +111,12 @@ class DeviceMesh:
     def is_distributed(self) -> bool:
         return self.mesh.numel() > 1
 
+    def has_dim_name(self, dim_name: str) -> bool:
+        return dim_name in self.dim_names
+
+    def dim_name_index(self, dim_name: str, default_value: Optional[int] = None) -> Optional[int]:
+        return self.dim_names.index(dim_name) if dim_name in self.dim_names else default_value
+
     def __eq__(self, other) -> bool:
         return isinstance(other, DeviceMesh) and torch.equal(self.mesh, other.mesh)
 
@@ -125,6 +131,44 @@ def init_device_mesh(device_type: str, mesh_shape: Union[int, Sequence[int]],
         mesh_shape = (mesh_shape,)
     mesh_shape = [s for s in mesh_shape if s is not None] or [1]
     return DeviceMesh(device_type, torch.arange(math.prod(mesh_shape)).view(mesh_shape), mesh_dim_names)
+
+
+def get_placements_from_dict(device_mesh: DeviceMesh, placements_dict: Dict[Union[str, int], Placement],
+                             original_placements: Optional[Sequence[Placement]] = None,
+                             default_placement_mode: str = "raise_error") -> List[Placement]:
+    """Placements per mesh dim from a dict keyed by mesh dim name or index (python/dtorch/distributed_spec.py:
+    233-305). Dims the dict does not name get Replicate ("replicate"), keep their current placement ("keep"),
+    or raise KeyError ("raise_error")."""
+    if default_placement_mode not in ("raise_error", "replicate", "keep"):
+        raise ValueError(f"unknown default_placement_mode {default_placement_mode!r}")
+    if device_mesh.ndim == 0:
+        return []
+    if default_placement_mode == "keep" and (original_placements is None
+                                            or len(original_placements) != device_mesh.ndim):
+        raise ValueError("default_placement_mode='keep' needs one original placement per mesh dim")
+    if not placements_dict:
+        if default_placement_mode == "replicate":
+            return [Replicate()] * device_mesh.ndim
+        if default_placement_mode == "keep":
+            return list(original_placements)
+        raise KeyError("placements_dict is empty and default_placement_mode is 'raise_error'")
+    by_name = all(isinstance(k, str) for k in placements_dict)
+    if not by_name and not all(isinstance(k, int) for k in placements_dict):
+        raise TypeError("placements_dict keys must be all mesh dim names or all mesh dim indices")
+    if by_name and len(device_mesh.dim_names) != device_mesh.ndim:
+        raise ValueError("placements_dict is keyed by dim name but the device mesh has no dim names")
+    out = []
+    for i in range(device_mesh.ndim):
+        key = device_mesh.dim_names[i] if by_name else i
+        if key in placements_dict:
+            out.append(placements_dict[key])
+        elif default_placement_mode == "replicate":
+            out.append(Replicate())
+        elif default_placement_mode == "keep":
+            out.append(original_placements[i])
+        else:
+            raise KeyError(f"mesh dim {key!r} is not in placements_dict {placements_dict}")
+    return out
 
 
 def cuda_device_of(global_id: int) -> int:
@@ -270,6 +314,26 @@ class DTensor:
 
     def redistribute_like(self, other: "DTensor") -> "DTensor":
         return self.redistribute(device_mesh=other.device_mesh, placements=other.placements)
+
+    def redistribute_by_dict(self, device_mesh: Optional[DeviceMesh] = None,
+                             placements_dict: Optional[Dict[Union[str, int], Placement]] = None, *,
+                             default_placement_mode: str = "raise_error",
+                             convert_shard_size_one_to_replicate: bool = True) -> "DTensor":
+        """Tensor.redistribute_by_dict (python/dtorch/tensor.py:317-351): placements named per mesh dim; a
+        Shard of a tensor dim of size 1 becomes Replicate unless told otherwise."""
+        device_mesh = device_mesh if device_mesh is not None else self.device_mesh
+        if placements_dict:
+            if device_mesh.is_distributed:
+                placements = get_placements_from_dict(device_mesh, placements_dict, self.placements,
+                                                      default_placement_mode)
+            else:
+                placements = [Replicate()] * device_mesh.ndim
+        else:
+            placements = list(self.placements)
+        if convert_shard_size_one_to_replicate:
+            placements = [Replicate() if p.is_shard() and self.shape[p.get_shard_index()] == 1 else p
+                          for p in placements]
+        return self.redistribute(device_mesh=device_mesh, placements=placements)
 
     def view(self, placements: Sequence[Placement]) -> "DTensor":
         """Tensor.view(placements) (python/dtorch/tensor.py:439-447): the same local tensors read under other

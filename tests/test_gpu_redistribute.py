@@ -358,3 +358,19 @@ def test_ulysses_and_ring_attention_on_2d_mesh(mode, overlap):
     torch.cuda.synchronize()
     assert out.placements == pl
     assert torch.allclose(out.to_torch(), want, rtol=1e-4, atol=1e-5)
+
+
+def test_redistribute_by_dict(mode):
+    # python/dtorch/tensor.py:317-351: placements by mesh dim name, the rest kept; a shard of a size-1 dim becomes
+    # Replicate
+    need(mode, 4)
+    mesh = dtb.init_device_mesh("cuda", (2, 2), mesh_dim_names=["dp", "tp"])
+    g = torch.Generator().manual_seed(15)
+    full = torch.randn(1, 12, 10, generator=g)
+    x = dtb.DTensor.from_torch(full, mesh, [dtb.Shard(1), dtb.Shard(2)])
+    y = x.redistribute_by_dict(placements_dict={"tp": dtb.Replicate()}, default_placement_mode="keep")
+    z = x.redistribute_by_dict(placements_dict={"dp": dtb.Shard(0), "tp": dtb.Shard(2)})
+    torch.cuda.synchronize()
+    assert y.placements == [dtb.Shard(1), dtb.Replicate()]
+    assert z.placements == [dtb.Replicate(), dtb.Shard(2)]  # Shard(0) of a size-1 dim -> Replicate
+    assert torch.equal(y.to_torch(), full) and torch.equal(z.to_torch(), full)

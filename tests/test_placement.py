@@ -143,3 +143,22 @@ def test_local_shapes_match_restatement_on_random_meshes():
         assert got == _local_shapes_restated(shape, mesh_shape, ids, placements)
 
     check()
+
+
+def test_placements_from_dict():
+    # python/dtorch/distributed_spec.py:233-305
+    import dtorch_b200 as dtb
+    mesh = dtb.init_device_mesh("cuda", (2, 2), mesh_dim_names=["dp", "cp"])
+    S, R = dtb.Shard, dtb.Replicate
+    assert dtb.get_placements_from_dict(mesh, {"dp": S(0), "cp": S(1)}) == [S(0), S(1)]
+    assert dtb.get_placements_from_dict(mesh, {1: S(2)}, default_placement_mode="replicate") == [R(), S(2)]
+    assert dtb.get_placements_from_dict(mesh, {"cp": S(2)}, [S(0), R()], "keep") == [S(0), S(2)]
+    assert dtb.get_placements_from_dict(mesh, {}, default_placement_mode="replicate") == [R(), R()]
+    with pytest.raises(KeyError):
+        dtb.get_placements_from_dict(mesh, {"dp": S(0)})
+    with pytest.raises(KeyError):
+        dtb.get_placements_from_dict(mesh, {})
+    with pytest.raises(TypeError):
+        dtb.get_placements_from_dict(mesh, {"dp": S(0), 1: R()})
+    with pytest.raises(ValueError):
+        dtb.get_placements_from_dict(dtb.init_device_mesh("cuda", (2,)), {"dp": S(0)})
