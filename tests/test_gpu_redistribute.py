@@ -12,6 +12,7 @@ bit-exact, since moves are copies and the fp32 sums fold in the reference's orde
 oracle fold.
 """
 
+import math
 import os
 import threading
 
@@ -374,3 +375,18 @@ def test_redistribute_by_dict(mode):
     assert y.placements == [dtb.Shard(1), dtb.Replicate()]
     assert z.placements == [dtb.Replicate(), dtb.Shard(2)]  # Shard(0) of a size-1 dim -> Replicate
     assert torch.equal(y.to_torch(), full) and torch.equal(z.to_torch(), full)
+
+
+@pytest.mark.parametrize("mesh_shape", [(2, 2, 2), (2, 1, 2)])
+def test_redistribute_by_dim_name_like_reference(mode, mesh_shape):
+    # python/dtorch/test/test_distributed_tensor.py:408-439
+    need(mode, math.prod(mesh_shape))
+    mesh = dtb.init_device_mesh("cuda", mesh_shape, mesh_dim_names=["dp", "cp", "tp"])
+    g = torch.Generator().manual_seed(16)
+    full = torch.rand(2, 4, 8, generator=g)
+    x = dtb.DTensor.from_torch(full, mesh, [dtb.Replicate()] * 3)
+    y = x.redistribute_by_dict(placements_dict={"dp": dtb.Shard(0), "cp": dtb.Shard(1), "tp": dtb.Shard(1)})
+    torch.cuda.synchronize()
+    assert torch.equal(y.to_torch(), full)
+    cp = dtb.Shard(1) if mesh_shape[1] > 1 else dtb.Replicate()
+    assert y.placements == [dtb.Shard(0), cp, dtb.Shard(1)]
