@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import os
 import socket
+import tempfile
 
 import torch
 import torch.distributed as dist
@@ -36,7 +37,7 @@ def share_fd(fd: int, tag: str) -> int:
     """Hand rank 0's file descriptor to every other rank (SCM_RIGHTS over a Unix socket); returns this rank's
     descriptor (rank 0's own, or the received duplicate, which the caller closes)."""
     rank, n = dist.get_rank(), dist.get_world_size()
-    path = f"/tmp/dtb_{os.getuid()}_{os.environ.get('MASTER_PORT', '0')}_{tag}.sock"
+    path = os.path.join(tempfile.gettempdir(), f"dtb_{os.getuid()}_{os.environ.get('MASTER_PORT', '0')}_{tag}.sock")
     if rank == 0:
         if os.path.exists(path):
             os.unlink(path)
