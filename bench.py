@@ -535,7 +535,10 @@ def run_ours_multi(args, rank, world, local_rank):
     code = capi.dtype_code(dtype) if dtype in (torch.float32, torch.bfloat16, torch.float16) else 0
     # all-reduce: the two-shot P2P kernel (rank-order fold) on the heap buffers, and -- where the switch
     # supports it and it is faster (n >= 4) -- the NVLS kernel on buffers bound to a multicast object
-    algo = "p2p two-shot (rank-order fp32 fold)"
+    algo = {"all_reduce": "p2p two-shot (rank-order fp32 fold)",
+            "reduce_scatter": "p2p pull-reduce (rank-order fp32 fold)",
+            "all_gather": "p2p push (peer stores at the concat offset)",
+            "all_to_all": "p2p push (pack fused into the peer stores)"}[op]
     ar_flags = 0
     xp, yp = x, y
     if op == "all_reduce" and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
