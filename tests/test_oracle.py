@@ -85,3 +85,67 @@ def test_restatement_matches_live_reference(n):
         outs, _ = ref.all_to_all(parts, code, 0, 1)
         for a, b in zip(R.all_to_all(parts, 0, 1), outs):
             assert np.array_equal(a, b)
+
+
+@pytest.mark.skipif(not Reference.available(), reason="reference library not built here")
+def test_restatement_matches_live_reference_on_random_cases():
+    """Random group sizes, shapes, dims and dtypes, restricted to what the reference accepts (its debug asserts
+    end the process otherwise): every collective of the restatement equals the reference's own output."""
+    hyp = pytest.importorskip("hypothesis")
+    st = pytest.importorskip("hypothesis.strategies")
+    ref = Reference()
+
+    @hyp.settings(max_examples=60, deadline=None)
+    @hyp.given(st.data())
+    def check(data):
+        n = data.draw(st.integers(2, 8))
+        code = data.draw(st.sampled_from([0, 1, 2]))
+        dt = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}[code]
+        op = data.draw(st.sampled_from(["all_reduce", "reduce_scatter", "all_gather", "all_to_all"]))
+        ndim = data.draw(st.integers(1 if op != "all_to_all" else 2, 4))
+        shape = [data.draw(st.integers(1, 6)) for _ in range(ndim)]
+        g = torch.Generator().manual_seed(data.draw(st.integers(0, 2 ** 31 - 1)))
+        if op in ("all_reduce", "reduce_scatter"):
+            count = int(np.prod(shape)) * (n if op == "reduce_scatter" else 1)
+            ins = [raw_from_torch(torch.randn(count, generator=g).to(dt)) for _ in range(n)]
+            if op == "all_reduce":
+                outs, _ = ref.all_reduce(ins, code)
+                want = [R.fold_sum(ins, code, True).reshape(-1)] * n
+            else:
+                outs, _ = ref.reduce_scatter(ins, code)
+                want = R.reduce_scatter(ins, code, True)
+            for a, b in zip(want, outs):
+                assert np.array_equal(np.asarray(a).reshape(-1), b.reshape(-1))
+            return
+        dim = data.draw(st.integers(0, ndim - 1))
+        length = data.draw(st.integers(n, 3 * n + 2))
+        lens = shard_sizes(length, n)
+        if op == "all_gather":
+            parts = []
+            for l in lens:
+                s = list(shape)
+                s[dim] = l
+                parts.append(raw_from_torch(torch.randn(*s, generator=g).to(dt)))
+            outs, _ = ref.all_gather(parts, code, dim)
+            want = R.all_gather(parts, dim)
+            for b in outs:
+                assert np.array_equal(want, b)
+            return
+        dst = data.draw(st.sampled_from([d for d in range(ndim) if d != dim]))
+        parts = []
+        for l in lens:
+            s = list(shape)
+            s[dim] = l
+            s[dst] = max(s[dst], n) + data.draw(st.integers(0, 3)) if l == lens[0] else s[dst]
+            parts.append(s)
+        dst_len = parts[0][dst]
+        tensors = []
+        for s in parts:
+            s = list(s)
+            s[dst] = dst_len
+            tensors.append(raw_from_torch(torch.randn(*s, generator=g).to(dt)))
+        outs, _ = ref.all_to_all(tensors, code, dim, dst)
+        for a, b in zip(R.all_to_all(tensors, dim, dst), outs):
+            assert np.array_equal(a, b)
+
+    check()
