@@ -112,6 +112,67 @@ def test_comm_golden(case, mode):
         comm.destroy()
 
 
+def _random_case(rng, n):
+    """One seeded random collective (op, dtype, shape, dims, uneven shards) with the restatement's answer."""
+    op = str(rng.choice(["all_reduce", "reduce_scatter", "all_gather", "all_to_all"]))
+    dt = str(rng.choice(["float32", "bfloat16", "float16"]))
+    td = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}[dt]
+    g = torch.Generator().manual_seed(int(rng.integers(1 << 30)))
+
+    def tensor(shape):
+        return raw_from_torch(torch.randn(*shape, generator=g).to(td))
+
+    meta = {"n": n, "op": op, "dtype": dt}
+    if op in ("all_reduce", "reduce_scatter"):
+        count = int(rng.integers(1, 3000)) * (n if op == "reduce_scatter" else 1)
+        ins = [tensor([count]) for _ in range(n)]
+        want = ([R.fold_sum(ins, DT_CODE[dt], False)] * n if op == "all_reduce"
+                else R.reduce_scatter(ins, DT_CODE[dt], False))
+        return meta, ins, want
+    ndim = int(rng.integers(1 if op == "all_gather" else 2, 5))
+    shape = [int(rng.integers(1, 9)) for _ in range(ndim)]
+    dim = int(rng.integers(ndim))
+    lens = shard_sizes(int(rng.integers(n, 4 * n + 3)), n)
+    if op == "all_gather":
+        ins = []
+        for l in lens:
+            s = list(shape)
+            s[dim] = l
+            ins.append(tensor(s))
+        meta["dim"] = dim
+        return meta, ins, [R.all_gather(ins, dim)] * n
+    dd = int(rng.choice([d for d in range(ndim) if d != dim]))
+    shape[dd] = max(shape[dd], n) + int(rng.integers(0, 3))
+    ins = []
+    for l in lens:
+        s = list(shape)
+        s[dim] = l
+        ins.append(tensor(s))
+    meta["src_dim"], meta["dst_dim"] = dim, dd
+    return meta, ins, R.all_to_all(ins, dim, dd)
+
+
+@pytest.mark.parametrize("mode", ["same", "peer"])
+@pytest.mark.parametrize("n", [2, 3, 4, 8])
+def test_comm_random_cases_match_restatement(mode, n):
+    """Seeded random collectives (ops, dtypes, ranks of 1-4 dims, every dim pair, uneven shards, odd sizes)
+    through the C ABI: gathers and all-to-alls bit-exact, reductions bit-exact against the fp32-accumulate
+    restatement."""
+    devs = devices_for(n, mode)
+    rng = np.random.default_rng(1000 + n)
+    comm = capi.Comm(devs)
+    try:
+        comm.set_timeout_ms(20000)
+        for i in range(24):
+            meta, ins, want = _random_case(rng, n)
+            got = run_case(comm, devs, meta, ins, flags=0)
+            for r in range(n):
+                assert np.array_equal(got[r], np.asarray(want[r]).reshape(-1)), (i, meta, r)
+        assert comm.error(0) == capi.DT_OK
+    finally:
+        comm.destroy()
+
+
 @pytest.mark.parametrize("algo", [capi.DT_ALGO_ONESHOT, capi.DT_ALGO_TWOSHOT])
 @pytest.mark.parametrize("count", [1, 7, 4096 + 3, (1 << 21) + 9])
 def test_peer_all_reduce_algorithms(algo, count):
