@@ -60,6 +60,7 @@ SIGNATURES = [
     ("dt_all_to_all", _I, [_P, _I, _P, _P, _I, _P, _I, _I, _P, _SZ, _P]),
     ("dt_barrier", _I, [_P, _I, _P]),
     ("dt_local_all_reduce", _I, [_I, _P, _P, _SZ, _I, _I, _P]),
+    ("dt_local_all_reduce_host", _I, [_I, _P, _P, _P, _P, _SZ, _I, _I, _SZ, _P]),
     ("dt_local_reduce_scatter", _I, [_I, _P, _P, _SZ, _I, _I, _P]),
     ("dt_local_all_gather", _I, [_I, _P, _P, _SZ, _P, _SZ, _P]),
     ("dt_local_all_to_all", _I, [_I, _P, _P, _I, _P, _I, _I, _P, _SZ, _P]),
@@ -256,6 +257,13 @@ class Comm:
 # ---- same-device kernels ----
 def local_all_reduce(ins, out, count, dtype, flags=0, stream=0):
     check(lib().dt_local_all_reduce(len(ins), ptr_array(ins), out, count, dtype, flags, stream), "dt_local_all_reduce")
+
+
+def local_all_reduce_host(host_ins, dev_ins, dev_out, host_out, count, dtype, flags=0, chunk_bytes=0, stream=0):
+    """Same-device all-reduce of pinned host partials, staged through device buffers chunk by chunk with the
+    copies in both directions overlapping the reduction; host_out is complete when `stream` reaches the call's end."""
+    check(lib().dt_local_all_reduce_host(len(host_ins), ptr_array(host_ins), ptr_array(dev_ins), dev_out, host_out,
+                                         count, dtype, flags, chunk_bytes, stream), "dt_local_all_reduce_host")
 
 
 def local_reduce_scatter(ins, outs, out_count, dtype, flags=0, stream=0):

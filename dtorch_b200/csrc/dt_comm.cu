@@ -19,6 +19,7 @@
 #include <string>
 #include <thread>
 #include <unordered_map>
+#include <memory>
 #include <vector>
 
 #include <cuda.h>
@@ -839,6 +840,26 @@ int local_reduce(int n, const char* const* ins, char* const* outs, int nout, siz
     return launch_reduce<false>(a, dtype, (flags & DT_ACCUM_STORAGE) != 0, dev, num_sms, stream);
 }
 
+// Copy streams and events of the host-buffer all-reduce, one set per device; the mutex serialises the
+// enqueueing of concurrent calls on one device (the events are reused from call to call).
+struct Staging {
+    std::mutex mu;
+    cudaStream_t h2d = nullptr;
+    cudaStream_t d2h = nullptr;
+    cudaEvent_t start = nullptr;
+    cudaEvent_t end = nullptr;
+    std::vector<cudaEvent_t> ev;  // 2 per chunk: inputs arrived, chunk reduced
+};
+
+Staging& staging_of(int dev) {
+    static std::mutex m;
+    static std::unordered_map<int, std::unique_ptr<Staging>> all;
+    std::lock_guard<std::mutex> g(m);
+    auto& p = all[dev];
+    if (!p) p = std::make_unique<Staging>();
+    return *p;
+}
+
 int current_device_sms(int* dev, int* sms) {
     DT_CUDA(cudaGetDevice(dev));
     DT_CUDA(cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, *dev));
@@ -1643,6 +1664,62 @@ int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, 
     for (int r = 0; r < n; ++r) in_c[r] = static_cast<const char*>(ins[r]);
     char* o = static_cast<char*>(out);
     return local_reduce(n, in_c, &o, 1, count, dtype, flags, static_cast<cudaStream_t>(stream), dev, sms);
+}
+
+int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* dev_ins, void* dev_out, void* host_out,
+                             size_t count, int dtype, int flags, size_t chunk_bytes, void* stream_v) {
+    if (n < 1 || n > kMaxRanks || host_ins == nullptr || dev_ins == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    const int es = elem_bytes(dtype);
+    if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
+    if (count == 0) return DT_OK;
+    if (dev_out == nullptr || host_out == nullptr) return fail(DT_ERR_INVALID, "null output");
+    for (int r = 0; r < n; ++r)
+        if (host_ins[r] == nullptr || dev_ins[r] == nullptr) return fail(DT_ERR_INVALID, "null input");
+    int dev = 0, sms = 0;
+    int st = current_device_sms(&dev, &sms);
+    if (st != DT_OK) return st;
+    cudaStream_t user = static_cast<cudaStream_t>(stream_v);
+    if (chunk_bytes == 0) chunk_bytes = static_cast<size_t>(4) << 20;
+    size_t chunk = std::max<size_t>(16, chunk_bytes / 16 * 16) / static_cast<size_t>(es);
+    const size_t nchunks = (count + chunk - 1) / chunk;
+    Staging& sg = staging_of(dev);
+    std::lock_guard<std::mutex> lock(sg.mu);
+    if (sg.h2d == nullptr) {
+        DT_CUDA(cudaStreamCreateWithFlags(&sg.h2d, cudaStreamNonBlocking));
+        DT_CUDA(cudaStreamCreateWithFlags(&sg.d2h, cudaStreamNonBlocking));
+        DT_CUDA(cudaEventCreateWithFlags(&sg.start, cudaEventDisableTiming));
+        DT_CUDA(cudaEventCreateWithFlags(&sg.end, cudaEventDisableTiming));
+    }
+    while (sg.ev.size() < 2 * nchunks) {
+        cudaEvent_t e;
+        DT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        sg.ev.push_back(e);
+    }
+    // the staging buffers are free once the work already on `stream` (earlier calls included) has finished
+    DT_CUDA(cudaEventRecord(sg.start, user));
+    DT_CUDA(cudaStreamWaitEvent(sg.h2d, sg.start, 0));
+    DT_CUDA(cudaStreamWaitEvent(sg.d2h, sg.start, 0));
+    for (size_t c = 0; c < nchunks; ++c) {
+        const size_t off = c * chunk * es;
+        const size_t len = std::min(chunk, count - c * chunk);
+        const char* ins_c[kMaxRanks];
+        for (int r = 0; r < n; ++r) {
+            DT_CUDA(cudaMemcpyAsync(static_cast<char*>(dev_ins[r]) + off, static_cast<const char*>(host_ins[r]) + off,
+                                    len * es, cudaMemcpyHostToDevice, sg.h2d));
+            ins_c[r] = static_cast<const char*>(dev_ins[r]) + off;
+        }
+        DT_CUDA(cudaEventRecord(sg.ev[2 * c], sg.h2d));
+        DT_CUDA(cudaStreamWaitEvent(user, sg.ev[2 * c], 0));
+        char* o = static_cast<char*>(dev_out) + off;
+        st = local_reduce(n, ins_c, &o, 1, len, dtype, flags, user, dev, sms);
+        if (st != DT_OK) return st;
+        DT_CUDA(cudaEventRecord(sg.ev[2 * c + 1], user));
+        DT_CUDA(cudaStreamWaitEvent(sg.d2h, sg.ev[2 * c + 1], 0));
+        DT_CUDA(cudaMemcpyAsync(static_cast<char*>(host_out) + off, o, len * es, cudaMemcpyDeviceToHost, sg.d2h));
+    }
+    DT_CUDA(cudaEventRecord(sg.end, sg.d2h));
+    DT_CUDA(cudaStreamWaitEvent(user, sg.end, 0));
+    return DT_OK;
 }
 
 int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, size_t out_count, int dtype, int flags,

@@ -198,6 +198,16 @@ int dt_comm_nvls_buffer(dt_comm* comm, int rank, void** ptr, size_t* bytes);
 /* out = rank-order sum of ins[0..n-1] (the fold of thread_group_same_device_backend.cc:224-228). */
 int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, int dtype, int flags, void* stream);
 
+/* The same all-reduce for partials that live in host memory (the reference's CPU-mesh all-reduce,
+ * ThreadGroup::AllReduce on kCpu tensors, thread_group.cc:127-141, run on one GPU): host_ins[r] (pinned) are
+ * copied in chunks into the device staging buffers dev_ins[r]; each chunk is reduced into dev_out as soon as
+ * all of its inputs have arrived and copied back into host_out (pinned) while later chunks are still on the
+ * way in, so both copy directions and the reduction overlap. Enqueued after the work already on `stream`;
+ * host_out is complete once `stream` reaches the end of the call. chunk_bytes: per-rank chunk size (0 = 4 MiB,
+ * rounded to 16 bytes). */
+int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* dev_ins, void* dev_out,
+                             void* host_out, size_t count, int dtype, int flags, size_t chunk_bytes, void* stream);
+
 /* outs[r] = rows [r*out_count, (r+1)*out_count) of the rank-order sum (same-device _reduce_scatter_base,
  * thread_group_same_device_backend.cc:238-274, without its in-place write into rank 0's input). */
 int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, size_t out_count, int dtype, int flags,

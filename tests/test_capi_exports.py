@@ -54,3 +54,12 @@ def test_all_to_all_rejects_dst_extent_below_group():
     lens = capi.i64_array([2, 2, 2, 2, 2, 1, 1, 1])
     assert L.dt_local_all_to_all(8, dummy, dummy, 4, shape, 2, 0, lens, 2, None) == capi.DT_ERR_INVALID
     assert b"dst dim" in L.dt_last_error_message()
+
+
+def test_host_buffer_all_reduce_rejects_bad_arguments():
+    L = capi.lib()
+    ptrs = capi.ptr_array([16] * 2)
+    assert L.dt_local_all_reduce_host(0, ptrs, ptrs, 16, 16, 8, 0, 0, 0, None) == capi.DT_ERR_INVALID
+    assert L.dt_local_all_reduce_host(2, ptrs, ptrs, 16, 16, 8, 7, 0, 0, None) == capi.DT_ERR_INVALID
+    assert L.dt_local_all_reduce_host(2, ptrs, ptrs, None, 16, 8, 0, 0, 0, None) == capi.DT_ERR_INVALID
+    assert L.dt_local_all_reduce_host(2, ptrs, ptrs, 16, 16, 0, 0, 0, 0, None) == capi.DT_OK  # nothing to do

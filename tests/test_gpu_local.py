@@ -123,3 +123,34 @@ def test_local_all_to_all_ulysses_shape():
     for k in range(n):
         off = sum(split[:k])
         assert torch.equal(d_out[k].cpu(), full[:, :, off:off + split[k]])
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("count,chunk", [(1000, 0), (100_003, 4096), ((1 << 20) + 5, 64 << 10)])
+def test_local_all_reduce_from_host_buffers(dt, count, chunk):
+    """dt_local_all_reduce_host: pinned host partials in, pinned host sum out, one reduction per chunk; two
+    back-to-back calls reuse the staging buffers in order."""
+    n = 8
+    code, td = DT_CODE[dt], TD[dt]
+    es = torch.tensor([], dtype=td).element_size()
+    g = torch.Generator().manual_seed(count)
+    hosts = [[torch.randn(count, generator=g).to(td).pin_memory() for _ in range(n)] for _ in range(2)]
+    dev = [torch.empty(count, dtype=td, device="cuda:0") for _ in range(n)]
+    dout = torch.empty(count, dtype=td, device="cuda:0")
+    houts = [torch.empty(count, dtype=td).pin_memory() for _ in range(2)]
+    s = torch.cuda.Stream(device=0)
+    n0 = launches()
+    for host, hout in zip(hosts, houts):
+        capi.local_all_reduce_host([h.data_ptr() for h in host], [d.data_ptr() for d in dev], dout.data_ptr(),
+                                   hout.data_ptr(), count, code, 0, chunk, s.cuda_stream)
+    s.synchronize()
+    chunk_elems = max(16, (chunk or (4 << 20)) // 16 * 16) // es
+    assert launches() - n0 == 2 * ((count + chunk_elems - 1) // chunk_elems)
+    for host, hout in zip(hosts, houts):
+        want = R.fold_sum([raw_from_torch(h) for h in host], code, storage_round=False)
+        assert np.array_equal(raw_from_torch(hout), want)
+    # reference rounding on request, as dt_local_all_reduce
+    capi.local_all_reduce_host([h.data_ptr() for h in hosts[0]], [d.data_ptr() for d in dev], dout.data_ptr(),
+                               houts[0].data_ptr(), count, code, capi.DT_ACCUM_STORAGE, chunk, s.cuda_stream)
+    s.synchronize()
+    assert np.array_equal(raw_from_torch(houts[0]), R.fold_sum([raw_from_torch(h) for h in hosts[0]], code, True))
