@@ -1679,7 +1679,9 @@ int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* de
     int st = current_device_sms(&dev, &sms);
     if (st != DT_OK) return st;
     cudaStream_t user = static_cast<cudaStream_t>(stream_v);
-    if (chunk_bytes == 0) chunk_bytes = static_cast<size_t>(4) << 20;
+    // 16 MiB per rank measured best for 8 x 128 MiB bf16 partials (4 MiB: per-copy overheads eat the overlap;
+    // 64 MiB and up: the last chunk's reduce and D2H no longer hide behind the inputs)
+    if (chunk_bytes == 0) chunk_bytes = static_cast<size_t>(16) << 20;
     size_t chunk = std::max<size_t>(16, chunk_bytes / 16 * 16) / static_cast<size_t>(es);
     const size_t nchunks = (count + chunk - 1) / chunk;
     Staging& sg = staging_of(dev);

@@ -203,7 +203,7 @@ int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, 
  * copied in chunks into the device staging buffers dev_ins[r]; each chunk is reduced into dev_out as soon as
  * all of its inputs have arrived and copied back into host_out (pinned) while later chunks are still on the
  * way in, so both copy directions and the reduction overlap. Enqueued after the work already on `stream`;
- * host_out is complete once `stream` reaches the end of the call. chunk_bytes: per-rank chunk size (0 = 4 MiB,
+ * host_out is complete once `stream` reaches the end of the call. chunk_bytes: per-rank chunk size (0 = 16 MiB,
  * rounded to 16 bytes). */
 int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* dev_ins, void* dev_out,
                              void* host_out, size_t count, int dtype, int flags, size_t chunk_bytes, void* stream);

@@ -144,7 +144,7 @@ def test_local_all_reduce_from_host_buffers(dt, count, chunk):
         capi.local_all_reduce_host([h.data_ptr() for h in host], [d.data_ptr() for d in dev], dout.data_ptr(),
                                    hout.data_ptr(), count, code, 0, chunk, s.cuda_stream)
     s.synchronize()
-    chunk_elems = max(16, (chunk or (4 << 20)) // 16 * 16) // es
+    chunk_elems = max(16, (chunk or (16 << 20)) // 16 * 16) // es
     assert launches() - n0 == 2 * ((count + chunk_elems - 1) // chunk_elems)
     for host, hout in zip(hosts, houts):
         want = R.fold_sum([raw_from_torch(h) for h in host], code, storage_round=False)
