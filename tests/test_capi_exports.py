@@ -4,6 +4,10 @@ with the signature table of the Python binding covering exactly those entry poin
 import ctypes
 import os
 import re
+import shutil
+import subprocess
+
+import pytest
 
 from dtorch_b200 import capi
 
@@ -63,3 +67,25 @@ def test_host_buffer_all_reduce_rejects_bad_arguments():
     assert L.dt_local_all_reduce_host(2, ptrs, ptrs, 16, 16, 8, 7, 0, 0, None) == capi.DT_ERR_INVALID
     assert L.dt_local_all_reduce_host(2, ptrs, ptrs, None, 16, 8, 0, 0, 0, None) == capi.DT_ERR_INVALID
     assert L.dt_local_all_reduce_host(2, ptrs, ptrs, 16, 16, 0, 0, 0, 0, None) == capi.DT_OK  # nothing to do
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """A C program (no C++, no torch) includes the header, links the library and makes host-only calls: the
+    boundary is a plain C ABI."""
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "abi.c"
+    src.write_text(
+        '#include <stdio.h>\n#include "dtorch_b200.h"\n'
+        "int main(void) {\n"
+        "  dt_comm* c = 0;\n"
+        "  if (dt_comm_create(0, 0, 0, &c) != DT_ERR_INVALID) return 1;\n"
+        '  printf("%d %s\\n", dt_version() >> 16, dt_status_string(DT_ERR_TIMEOUT));\n'
+        "  return 0;\n}\n")
+    exe = tmp_path / "abi"
+    libdir = os.path.dirname(capi.LIB_PATH)
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", f"-I{os.path.dirname(HEADER)}", str(src), "-o", str(exe),
+                    f"-L{libdir}", "-ldtorch_b200", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    assert out.strip() == "1 timeout waiting for a peer"
