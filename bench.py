@@ -874,80 +874,6 @@ def run_sweep_single(args):
                 del ins, outs
 
 
-# ---------------------------------------------------------------------------------------------------------
-# --link-probe: what one GPU pair sustains per direction with each transfer mechanism (diagnostic)
-# ---------------------------------------------------------------------------------------------------------
-def run_link_probe(args):
-    import ctypes
-
-    lib = ctypes.CDLL(os.path.join(ROOT, "dtorch_b200", "_lib", "libdtorch_b200_probe.so"))
-    P = ctypes.c_void_p
-    lib.probe_lsu.argtypes = [P, P, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, P]
-    lib.probe_tma.argtypes = [P, P, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P]
-    assert torch.cuda.device_count() >= 2, "--link-probe needs two GPUs"
-    for d in (0, 1):
-        lib.probe_set_device(d)
-        assert lib.probe_prepare() == 0
-    assert lib.probe_enable_peer(0, 1) == 0 and lib.probe_enable_peer(1, 0) == 0
-    gib = 1 << 30
-    buf = {d: (torch.empty(gib, dtype=torch.uint8, device=f"cuda:{d}"), torch.empty(gib, dtype=torch.uint8, device=f"cuda:{d}"))
-           for d in (0, 1)}
-    for d in (0, 1):
-        buf[d][0].random_(0, 255)
-    err = {d: torch.zeros(1, dtype=torch.int32, device=f"cuda:{d}") for d in (0, 1)}
-
-    def run(method, cfg, nbytes, bidir, push=True, iters=10):
-        pairs = [(0, 1), (1, 0)] if bidir else [(0, 1)]
-
-        def launch(src_dev, dst_dev):
-            kdev = src_dev if push else dst_dev
-            src, dst = buf[src_dev][0].data_ptr(), buf[dst_dev][1].data_ptr()
-            st = torch.cuda.current_stream(kdev).cuda_stream
-            lib.probe_set_device(kdev)
-            if method == "lsu":
-                rc = lib.probe_lsu(src, dst, nbytes, cfg[0], cfg[1], st)
-            elif method == "tma":
-                rc = lib.probe_tma(src, dst, nbytes, cfg[0], cfg[1], cfg[2], err[kdev].data_ptr(), st)
-            else:
-                with torch.cuda.device(kdev):
-                    buf[dst_dev][1][:nbytes].copy_(buf[src_dev][0][:nbytes], non_blocking=True)
-                rc = 0
-            assert rc == 0, rc
-
-        for _ in range(2):
-            for a, b in pairs:
-                launch(a, b)
-        for d in (0, 1):
-            torch.cuda.synchronize(d)
-        kdevs = sorted(set((a if push else b) for a, b in pairs))
-        evs = {}
-        for d in kdevs:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(torch.cuda.current_stream(d))
-            evs[d] = (e0, e1)
-        for _ in range(iters):
-            for a, b in pairs:
-                launch(a, b)
-        for d in kdevs:
-            evs[d][1].record(torch.cuda.current_stream(d))
-        for d in (0, 1):
-            torch.cuda.synchronize(d)
-        assert int(err[0].item()) == 0 and int(err[1].item()) == 0
-        ms = max(evs[d][0].elapsed_time(evs[d][1]) for d in kdevs) / iters
-        return nbytes / ms / 1e6
-
-    for nb in (256 << 20, 1 << 30):
-        for bidir in (False, True):
-            rows = [("ce", None, "push")]
-            rows += [("lsu", c, d) for c in [(148, 512), (296, 512), (592, 512), (148, 1024)] for d in ("push", "pull")]
-            rows += [("tma", c, d) for c in [(148, 32768, 4), (296, 16384, 4), (148, 65536, 3), (148, 32768, 6),
-                                             (444, 8192, 8), (296, 32768, 4)] for d in ("push", "pull")]
-            for method, cfg, d in rows:
-                gbs = run(method, cfg, nb, bidir, d == "push")
-                print(json.dumps({"link_probe": method, "cfg": cfg, "MiB": nb >> 20, "bidir": bidir, "dir": d,
-                                  "GBps_per_dir": round(gbs, 1)}), flush=True)
-
-
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -960,8 +886,6 @@ def main():
     p.add_argument("--algo", choices=["auto", "p2p", "nvls"], default="auto",
                    help="all-reduce algorithm at N > 1: auto = NVLS where supported and n >= 4, else P2P two-shot")
     p.add_argument("--sweep", action="store_true", help="C5 message-size sweep, one JSON line per point")
-    p.add_argument("--link-probe", action="store_true", help="per-direction NVLink throughput of each transfer "
-                   "mechanism between GPU 0 and GPU 1 (diagnostic, one JSON line per point)")
     p.add_argument("--sweep-lo", type=int, default=10, help="smallest size, log2 bytes")
     p.add_argument("--sweep-hi", type=int, default=30, help="largest size, log2 bytes")
     p.add_argument("--sweep-ops", default="all_reduce,all_gather,reduce_scatter,all_to_all")
@@ -973,9 +897,6 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
-        return
-    if args.link_probe:
-        run_link_probe(args)
         return
     if args.sweep:
         run_sweep_multi(args, rank, world, local_rank) if world > 1 else run_sweep_single(args)

@@ -98,24 +98,9 @@ def build_host(force: bool = False, verbose: bool = False) -> str:
     return out
 
 
-def build_probe(force: bool = False, verbose: bool = False) -> str:
-    """_lib/libdtorch_b200_probe.so: the NVLink transfer probe of `bench.py --link-probe` (diagnostic only)."""
-    os.makedirs(LIBDIR, exist_ok=True)
-    out = os.path.join(LIBDIR, "libdtorch_b200_probe.so")
-    src = os.path.join(CSRC, "probe", "link_probe.cu")
-    if force or _newer(out, [src]):
-        cmd = [nvcc(), *NVCC_FLAGS, *ARCH, "-shared", "-cudart", "static", "-o", out + ".tmp", src]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
-        os.replace(out + ".tmp", out)
-    return out
-
-
 def build_all(force: bool = False, verbose: bool = False) -> None:
     build_capi(force=force, verbose=verbose)
     build_host(force=force, verbose=verbose)
-    build_probe(force=force, verbose=verbose)
 
 
 if __name__ == "__main__":

@@ -841,14 +841,18 @@ int local_reduce(int n, const char* const* ins, char* const* outs, int nout, siz
 }
 
 // Copy streams and events of the host-buffer all-reduce, one set per device; the mutex serialises the
-// enqueueing of concurrent calls on one device (the events are reused from call to call).
+// enqueueing of concurrent calls on one device. Every event is waited on right after it is recorded, and
+// cudaStreamWaitEvent captures the record it sees at that moment, so one event per hand-off direction is
+// reused for every chunk of every call.
 struct Staging {
     std::mutex mu;
     cudaStream_t h2d = nullptr;
     cudaStream_t d2h = nullptr;
     cudaEvent_t start = nullptr;
-    cudaEvent_t end = nullptr;
-    std::vector<cudaEvent_t> ev;  // 2 per chunk: inputs arrived, chunk reduced
+    cudaEvent_t end_h2d = nullptr;
+    cudaEvent_t end_d2h = nullptr;
+    cudaEvent_t arrived = nullptr;  // a chunk's inputs are on the device (h2d -> caller's stream)
+    cudaEvent_t reduced = nullptr;  // a chunk's sum is ready (caller's stream -> d2h)
 };
 
 Staging& staging_of(int dev) {
@@ -1689,38 +1693,50 @@ int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* de
     if (sg.h2d == nullptr) {
         DT_CUDA(cudaStreamCreateWithFlags(&sg.h2d, cudaStreamNonBlocking));
         DT_CUDA(cudaStreamCreateWithFlags(&sg.d2h, cudaStreamNonBlocking));
-        DT_CUDA(cudaEventCreateWithFlags(&sg.start, cudaEventDisableTiming));
-        DT_CUDA(cudaEventCreateWithFlags(&sg.end, cudaEventDisableTiming));
-    }
-    while (sg.ev.size() < 2 * nchunks) {
-        cudaEvent_t e;
-        DT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        sg.ev.push_back(e);
+        for (cudaEvent_t* e : {&sg.start, &sg.end_h2d, &sg.end_d2h, &sg.arrived, &sg.reduced})
+            DT_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     }
     // the staging buffers are free once the work already on `stream` (earlier calls included) has finished
     DT_CUDA(cudaEventRecord(sg.start, user));
     DT_CUDA(cudaStreamWaitEvent(sg.h2d, sg.start, 0));
     DT_CUDA(cudaStreamWaitEvent(sg.d2h, sg.start, 0));
-    for (size_t c = 0; c < nchunks; ++c) {
+    int rc = DT_OK;
+    auto cuda_ok = [&rc](cudaError_t e, const char* what) {
+        if (e != cudaSuccess && rc == DT_OK) rc = fail(DT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+        return rc == DT_OK;
+    };
+    for (size_t c = 0; c < nchunks && rc == DT_OK; ++c) {
         const size_t off = c * chunk * es;
         const size_t len = std::min(chunk, count - c * chunk);
         const char* ins_c[kMaxRanks];
-        for (int r = 0; r < n; ++r) {
-            DT_CUDA(cudaMemcpyAsync(static_cast<char*>(dev_ins[r]) + off, static_cast<const char*>(host_ins[r]) + off,
-                                    len * es, cudaMemcpyHostToDevice, sg.h2d));
+        for (int r = 0; r < n && rc == DT_OK; ++r) {
+            cuda_ok(cudaMemcpyAsync(static_cast<char*>(dev_ins[r]) + off, static_cast<const char*>(host_ins[r]) + off,
+                                    len * es, cudaMemcpyHostToDevice, sg.h2d),
+                    "cudaMemcpyAsync H2D");
             ins_c[r] = static_cast<const char*>(dev_ins[r]) + off;
         }
-        DT_CUDA(cudaEventRecord(sg.ev[2 * c], sg.h2d));
-        DT_CUDA(cudaStreamWaitEvent(user, sg.ev[2 * c], 0));
+        if (!cuda_ok(cudaEventRecord(sg.arrived, sg.h2d), "cudaEventRecord")) break;
+        if (!cuda_ok(cudaStreamWaitEvent(user, sg.arrived, 0), "cudaStreamWaitEvent")) break;
         char* o = static_cast<char*>(dev_out) + off;
-        st = local_reduce(n, ins_c, &o, 1, len, dtype, flags, user, dev, sms);
-        if (st != DT_OK) return st;
-        DT_CUDA(cudaEventRecord(sg.ev[2 * c + 1], user));
-        DT_CUDA(cudaStreamWaitEvent(sg.d2h, sg.ev[2 * c + 1], 0));
-        DT_CUDA(cudaMemcpyAsync(static_cast<char*>(host_out) + off, o, len * es, cudaMemcpyDeviceToHost, sg.d2h));
+        rc = local_reduce(n, ins_c, &o, 1, len, dtype, flags, user, dev, sms);
+        if (rc != DT_OK) break;
+        if (!cuda_ok(cudaEventRecord(sg.reduced, user), "cudaEventRecord")) break;
+        if (!cuda_ok(cudaStreamWaitEvent(sg.d2h, sg.reduced, 0), "cudaStreamWaitEvent")) break;
+        cuda_ok(cudaMemcpyAsync(static_cast<char*>(host_out) + off, o, len * es, cudaMemcpyDeviceToHost, sg.d2h),
+                "cudaMemcpyAsync D2H");
     }
-    DT_CUDA(cudaEventRecord(sg.end, sg.d2h));
-    DT_CUDA(cudaStreamWaitEvent(user, sg.end, 0));
+    // whether or not every chunk was enqueued, `stream` ends after every copy this call put in flight, so a
+    // caller that synchronizes `stream` after an error may free or reuse the buffers
+    const std::string msg = g_err;
+    const bool ends_ok = cudaEventRecord(sg.end_h2d, sg.h2d) == cudaSuccess &&
+                         cudaEventRecord(sg.end_d2h, sg.d2h) == cudaSuccess &&
+                         cudaStreamWaitEvent(user, sg.end_h2d, 0) == cudaSuccess &&
+                         cudaStreamWaitEvent(user, sg.end_d2h, 0) == cudaSuccess;
+    if (rc != DT_OK) {
+        g_err = msg;
+        return rc;
+    }
+    if (!ends_ok) return fail(DT_ERR_CUDA, "dt_local_all_reduce_host: ordering the caller's stream after the copies");
     return DT_OK;
 }
 

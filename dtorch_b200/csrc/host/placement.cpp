@@ -165,7 +165,7 @@ std::map<int64_t, std::vector<int64_t>> ComputeLocalShapes(const std::vector<int
     for (const auto& kv : infos) {
         const size_t d = static_cast<size_t>(kv.first);
         // sub-split Shard(d, s) on one mesh dim: piece i = piece i of the first s + 1 rows plus piece i of the
-        // rest (ReplicateToShard, thread_group.cc:339-358; DistributedScather, distributed_scather_and_gather.cc:61-80)
+        // rest (ReplicateToShard, thread_group.cc:258-276; DistributedScather, distributed_scather_and_gather.cc:61-80)
         int64_t sub = -1;
         for (auto md : kv.second.meshDims)
             if (p[md].HasSubSplit()) sub = p[md].subSplit;

@@ -46,13 +46,13 @@ typedef enum dt_dtype {
 } dt_dtype;
 
 typedef enum dt_redop {
-    DT_SUM = 0 /* c10d::ReduceOp::SUM; the only op the reference asserts (thread_group.cc:212, :283) */
+    DT_SUM = 0 /* c10d::ReduceOp::SUM; the only op the reference asserts (thread_group.cc:130, :201) */
 } dt_redop;
 
 /* Reduction flags (bitwise OR).
  *   DT_ACCUM_FP32     accumulate in fp32 in rank order 0..n-1, round to the storage type once (default).
  *   DT_ACCUM_STORAGE  round to the storage type after every add, which is what the reference's CPU fold
- *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:224-228);
+ *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:123-130);
  *                     bit-identical to it. For fp32 both modes are the same left fold.
  *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size.
  *   DT_ALGO_NVLS      reduce inside the NVSwitch (NVLink SHARP): needs input and output in the communicator's
@@ -195,7 +195,7 @@ int dt_comm_nvls_buffer(dt_comm* comm, int rank, void** ptr, size_t* bytes);
  * every rank's buffer (the 1-GPU emulation mode, DTORCH_DTENSOR_IN_SAME_DEVICE in the reference) can use them
  * directly. `ins`/`outs` are host arrays of n device pointers. */
 
-/* out = rank-order sum of ins[0..n-1] (the fold of thread_group_same_device_backend.cc:224-228). */
+/* out = rank-order sum of ins[0..n-1] (the fold of thread_group_same_device_backend.cc:123-130). */
 int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, int dtype, int flags, void* stream);
 
 /* The same all-reduce for partials that live in host memory (the reference's CPU-mesh all-reduce,
@@ -204,7 +204,12 @@ int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, 
  * all of its inputs have arrived and copied back into host_out (pinned) while later chunks are still on the
  * way in, so both copy directions and the reduction overlap. Enqueued after the work already on `stream`;
  * host_out is complete once `stream` reaches the end of the call. chunk_bytes: per-rank chunk size (0 = 16 MiB,
- * rounded to 16 bytes). */
+ * rounded to 16 bytes; chunks are 16 bytes at least).
+ * In place is allowed on both sides: dev_out may equal one of dev_ins[r] and host_out one of host_ins[r] (a
+ * chunk's result is written only after all of that chunk's inputs were read). Calls that share staging buffers
+ * must be issued on the same stream: a call waits only for earlier work on its own stream. If the call fails
+ * part way, `stream` still ends after every copy it had put in flight, so synchronizing `stream` makes the
+ * buffers safe to free or reuse. */
 int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* dev_ins, void* dev_out,
                              void* host_out, size_t count, int dtype, int flags, size_t chunk_bytes, void* stream);
 

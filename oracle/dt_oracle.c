@@ -5,14 +5,14 @@
  * nothing in the product links or calls it.
  *
  * Reference being restated (tingkuanpei/dtorch):
- *   all-reduce      dtorch/core/communication/thread_group/thread_group_same_device_backend.cc:209-244
+ *   all-reduce      dtorch/core/communication/thread_group/thread_group_same_device_backend.cc:111-146
  *                   rank 0 folds result = in_0; result += in_r for r = 1..n-1 (torch CPU add_ in the tensor's
  *                   dtype: each partial sum is rounded to the storage type), every rank gets that tensor.
- *   all-gather      thread_group_same_device_backend.cc:301-334 (_allgather_base: concat along dim 0 in rank
- *                   order) and :275-299 + thread_group.cc:250-253 (allgather list + torch::concat(dim)).
- *   reduce-scatter  thread_group_same_device_backend.cc:336-372: the same fold over the full tensor, then
+ *   all-gather      thread_group_same_device_backend.cc:203-236 (_allgather_base: concat along dim 0 in rank
+ *                   order) and :177-201 + thread_group.cc:168-190 (allgather list + torch::concat(dim)).
+ *   reduce-scatter  thread_group_same_device_backend.cc:238-274: the same fold over the full tensor, then
  *                   torch::chunk(n, 0)[rank].
- *   all-to-all      thread_group.cc:293-323: split(input, GetShardSizeForAllRank(size(dst), n), dst), chunk k
+ *   all-to-all      thread_group.cc:211-241: split(input, GetShardSizeForAllRank(size(dst), n), dst), chunk k
  *                   to rank k, concat(received, src) in rank order.
  *   shard sizes     dtorch/api/cpp/distributed_spec.cc:202-213: the first L % n ranks get floor(L/n) + 1.
  *
@@ -140,7 +140,7 @@ void oracle_shard_sizes(int64_t L, int n, int64_t* out) {
 
 /* ---- collectives ------------------------------------------------------------------------------------------ */
 
-/* Rank-order fold of n buffers of `count` elements (thread_group_same_device_backend.cc:222-228). */
+/* Rank-order fold of n buffers of `count` elements (thread_group_same_device_backend.cc:123-130). */
 void oracle_fold_sum(int n, const void* const* ins, void* out, size_t count, int dtype, int storage_round) {
     for (size_t i = 0; i < count; ++i) {
         float acc = load_elem(ins[0], i, dtype);
@@ -154,7 +154,7 @@ void oracle_fold_sum(int n, const void* const* ins, void* out, size_t count, int
 }
 
 /* Reduce-scatter: fold of the full inputs, rank k keeps rows [k*out_count, (k+1)*out_count)
- * (thread_group_same_device_backend.cc:336-372; torch::chunk of an evenly divisible dim 0). */
+ * (thread_group_same_device_backend.cc:238-274; torch::chunk of an evenly divisible dim 0). */
 void oracle_reduce_scatter(int n, const void* const* ins, void* const* outs, size_t out_count, int dtype,
                            int storage_round) {
     const size_t es = dtype == 0 ? 4 : 2;
@@ -182,7 +182,7 @@ void oracle_all_gather(int n, const void* const* ins, void* out, size_t outer, c
     }
 }
 
-/* All-to-all (thread_group.cc:293-323), element by element: for destination rank k and each element of its
+/* All-to-all (thread_group.cc:211-241), element by element: for destination rank k and each element of its
  * output, find the source rank i whose src-dim range holds the element's src coordinate, and read that rank's
  * input at the same coordinates except src (minus rank i's offset) and dst (plus chunk k's offset). */
 void oracle_all_to_all(int n, const void* const* ins, void* const* outs, int ndim, const int64_t* in_shape,

@@ -154,3 +154,21 @@ def test_local_all_reduce_from_host_buffers(dt, count, chunk):
                                houts[0].data_ptr(), count, code, capi.DT_ACCUM_STORAGE, chunk, s.cuda_stream)
     s.synchronize()
     assert np.array_equal(raw_from_torch(houts[0]), R.fold_sum([raw_from_torch(h) for h in hosts[0]], code, True))
+
+
+@pytest.mark.parametrize("chunk", [0, 4096])
+def test_local_all_reduce_from_host_buffers_in_place(chunk):
+    """dt_local_all_reduce_host with dev_out == dev_ins[2] and host_out == host_ins[1]: the sum lands in rank 1's
+    host partial and matches the rank-order fold of the original partials."""
+    n, count, dt = 4, 50_021, "bfloat16"
+    code, td = DT_CODE[dt], TD[dt]
+    g = torch.Generator().manual_seed(77)
+    host = [torch.randn(count, generator=g).to(td).pin_memory() for _ in range(n)]
+    want = R.fold_sum([raw_from_torch(h) for h in host], code, storage_round=False)
+    dev = [torch.empty(count, dtype=td, device="cuda:0") for _ in range(n)]
+    s = torch.cuda.Stream(device=0)
+    capi.local_all_reduce_host([h.data_ptr() for h in host], [d.data_ptr() for d in dev], dev[2].data_ptr(),
+                               host[1].data_ptr(), count, code, 0, chunk, s.cuda_stream)
+    s.synchronize()
+    assert np.array_equal(raw_from_torch(host[1]), want)
+    assert np.array_equal(np_raw(dev[2]), want)
