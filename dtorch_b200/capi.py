@@ -72,6 +72,7 @@ SIGNATURES = [
     ("dt_comm_nvls_attach", _I, [_P, _I, _SZ]),
     ("dt_comm_nvls_bind", _I, [_P]),
     ("dt_comm_nvls_buffer", _I, [_P, _I, _P, _P]),
+    ("dt_local_all_reduce_host_noalloc", _I, [_I, _P, _P, _SZ, _I, _I, _P]),
 ]
 
 
@@ -264,6 +265,18 @@ def local_all_reduce_host(host_ins, dev_ins, dev_out, host_out, count, dtype, fl
     copies in both directions overlapping the reduction; host_out is complete when `stream` reaches the call's end."""
     check(lib().dt_local_all_reduce_host(len(host_ins), ptr_array(host_ins), ptr_array(dev_ins), dev_out, host_out,
                                          count, dtype, flags, chunk_bytes, stream), "dt_local_all_reduce_host")
+
+
+NOALLOC_SCRATCH_BYTES = 32 << 20  # DT_NOALLOC_SCRATCH_BYTES
+
+
+def local_all_reduce_host_noalloc(host_ins, host_out, count, dtype, flags=0, stream=0):
+    """dt_local_all_reduce_host without staging buffers: the partials and the sum pass through the library's
+    fixed device scratch (NOALLOC_SCRATCH_BYTES per GPU), for callers that cannot allocate device memory.
+    (n + 1) slots of count * element size bytes, each rounded up to 256, must fit; calls that overlap on the
+    GPU race on the shared scratch."""
+    check(lib().dt_local_all_reduce_host_noalloc(len(host_ins), ptr_array(host_ins), host_out, count, dtype, flags,
+                                                 stream), "dt_local_all_reduce_host_noalloc")
 
 
 def local_reduce_scatter(ins, outs, out_count, dtype, flags=0, stream=0):

@@ -1831,3 +1831,79 @@ int dt_local_all_to_all(int n, const void* const* ins, void* const* outs, int nd
 }
 
 }  // extern "C"
+
+// =============================================================================================================
+// Host-partials all-reduce that allocates nothing on the device
+// =============================================================================================================
+// Staging memory of dt_local_all_reduce_host_noalloc: a fixed array in the library's own device image. Every
+// GPU on which the library's kernels are loaded holds these DT_NOALLOC_SCRATCH_BYTES until the process exits.
+// In host code this name is a host-side stand-in, not a device address: only the address that
+// cudaGetSymbolAddress returns for the current device may be handed to a kernel or a copy.
+static __device__ __align__(256) unsigned char dt_noalloc_scratch[DT_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of dt_noalloc_scratch on `dev` (which must be current), looked up once per device.
+int noalloc_scratch(int dev, char** out) {
+    static std::mutex mu;
+    static std::unordered_map<int, char*> addr;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = addr.find(dev);
+    if (it == addr.end()) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, dt_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return fail(DT_ERR_CUDA, std::string("cudaGetSymbolAddress(dt_noalloc_scratch): ") + cudaGetErrorString(e));
+        }
+        it = addr.emplace(dev, static_cast<char*>(p)).first;
+    }
+    *out = it->second;
+    return DT_OK;
+}
+
+size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" int dt_local_all_reduce_host_noalloc(int n, const void* const* host_ins, void* host_out, size_t count,
+                                                int dtype, int flags, void* stream_v) {
+    if (n < 1 || n > kMaxRanks || host_ins == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    const int es = elem_bytes(dtype);
+    if (es == 0) return fail(DT_ERR_INVALID, "unsupported dtype");
+    if (count == 0) return DT_OK;
+    if (host_out == nullptr) return fail(DT_ERR_INVALID, "null output");
+    for (int r = 0; r < n; ++r)
+        if (host_ins[r] == nullptr) return fail(DT_ERR_INVALID, "null input");
+    // n input slots and one output slot, each 256-byte aligned; checked before anything touches the device
+    const size_t slot = round256(count * static_cast<size_t>(es));
+    if (count > (static_cast<size_t>(DT_NOALLOC_SCRATCH_BYTES) / static_cast<size_t>(es)) ||
+        slot * static_cast<size_t>(n + 1) > static_cast<size_t>(DT_NOALLOC_SCRATCH_BYTES)) {
+        return fail(DT_ERR_INVALID, "dt_local_all_reduce_host_noalloc: " + std::to_string(n) + " partials of " +
+                                        std::to_string(count * static_cast<size_t>(es)) + " bytes need " +
+                                        std::to_string(n + 1) + " staging slots of " + std::to_string(slot) +
+                                        " bytes; the static scratch holds " +
+                                        std::to_string(static_cast<size_t>(DT_NOALLOC_SCRATCH_BYTES)) +
+                                        " bytes (use dt_local_all_reduce_host with caller-provided buffers)");
+    }
+    int dev = 0, sms = 0;
+    int st = current_device_sms(&dev, &sms);
+    if (st != DT_OK) return st;
+    char* scratch = nullptr;
+    st = noalloc_scratch(dev, &scratch);
+    if (st != DT_OK) return st;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    // Everything on the caller's stream: the inputs' copies, one rank-order reduction, the result's copy.
+    // Every scratch byte the reduction reads was written by this call's own copies, so nothing needs clearing.
+    const char* ins[kMaxRanks];
+    for (int r = 0; r < n; ++r) {
+        char* d = scratch + static_cast<size_t>(r) * slot;
+        DT_CUDA(cudaMemcpyAsync(d, host_ins[r], count * es, cudaMemcpyHostToDevice, stream));
+        ins[r] = d;
+    }
+    char* out = scratch + static_cast<size_t>(n) * slot;
+    st = local_reduce(n, ins, &out, 1, count, dtype, flags, stream, dev, sms);
+    if (st != DT_OK) return st;
+    DT_CUDA(cudaMemcpyAsync(host_out, out, count * es, cudaMemcpyDeviceToHost, stream));
+    return DT_OK;
+}

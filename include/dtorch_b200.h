@@ -213,6 +213,28 @@ int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, 
 int dt_local_all_reduce_host(int n, const void* const* host_ins, void* const* dev_ins, void* dev_out,
                              void* host_out, size_t count, int dtype, int flags, size_t chunk_bytes, void* stream);
 
+/* Size of the device scratch that dt_local_all_reduce_host_noalloc stages through (32 MiB). */
+#define DT_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* The host-partials all-reduce of dt_local_all_reduce_host for callers that cannot allocate device memory,
+ * with no staging buffers to pass in. No counterpart in the reference. It serves callers that hold host tensors
+ * only -- the CPU-mesh side of a ThreadGroup has no device buffers of its own to stage through -- and callers
+ * whose device memory is owned by another allocator (a serving process that reserved the GPU's memory up front)
+ * or that cannot afford cudaMalloc / cudaFree, which may synchronize the whole device.
+ * The n partials and the sum are staged in a fixed array inside this library's device image: every GPU on
+ * which the library's kernels are loaded holds DT_NOALLOC_SCRATCH_BYTES until the process exits, and the call
+ * itself calls no cudaMalloc, cudaFree or other allocating routine. The staging needs n + 1 slots of
+ * count * element size bytes, each rounded up to 256 bytes; anything larger is rejected with DT_ERR_INVALID
+ * before the device is touched. Runs on the current device; the first call on a device looks up the array's
+ * device address, so make that first call before any stream capture. Everything is enqueued on `stream` in
+ * order (copies in, one rank-order reduction, copy out; no overlap), and host_out is complete once `stream`
+ * reaches the end of the call. host_ins[r] and host_out should be pinned for asynchronous copies. Every call
+ * on a device shares the one array, which keeps the last call's contents: calls on one stream are ordered,
+ * but calls that overlap on the GPU (different streams, or different host threads) race on it.
+ * flags: DT_ACCUM_FP32 or DT_ACCUM_STORAGE, as for dt_local_all_reduce. */
+int dt_local_all_reduce_host_noalloc(int n, const void* const* host_ins, void* host_out, size_t count, int dtype,
+                                     int flags, void* stream);
+
 /* outs[r] = rows [r*out_count, (r+1)*out_count) of the rank-order sum (same-device _reduce_scatter_base,
  * thread_group_same_device_backend.cc:238-274, without its in-place write into rank 0's input). */
 int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, size_t out_count, int dtype, int flags,
