@@ -33,7 +33,7 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 NVLINK_NOMINAL_GBS = 900.0      # NVLink 5, per direction per GPU
-NVLINK_PEER_COPY_GBS = 770.0    # measured peer copy per direction on this pool (profiling recipe)
+NVLINK_P2P_CEILING_GBS = 709.0  # SM stores to a peer, both directions at once (profiles/nvlink_p2p_ceiling_probe.md)
 FALLBACK_HBM_GBS = 6650.0
 
 # ---------------------------------------------------------------------------------------------------------
@@ -165,6 +165,61 @@ class ClockSampler:
         names = [k for k, v in self.REASONS.items() if reasons & v and k != "gpu_idle"]
         return {"sm_mhz": statistics.median([s[1] for s in inside]), "sm_max_mhz": self.max_mhz,
                 "reasons": names, "samples": len(inside), "region_s": round(self.t1 - self.t0, 4)}
+
+
+# ---------------------------------------------------------------------------------------------------------
+# NVLink traffic counters (NVML field values, read-only): payload bytes this GPU sent and received over all of
+# its NVLinks. Read before and after the timed steps, they give the traffic of the collective per launch.
+# ---------------------------------------------------------------------------------------------------------
+class NvLinkCounter:
+    FI_TX, FI_RX = 138, 139  # NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX / _RX, in KiB
+    MAX_LINKS = 18
+
+    def __init__(self, cuda_index: int):
+        self.h = None
+        self.scope = None
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv = nv
+            try:
+                p = torch.cuda.get_device_properties(cuda_index)
+                bus = "%08x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+                self.h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = nv.nvmlDeviceGetHandleByIndex(cuda_index)
+            # aggregate over links if the driver offers it, else the sum of the per-link counters
+            for scope in ([0xFFFFFFFF], list(range(self.MAX_LINKS))):
+                if self._read(scope) is not None:
+                    self.scope = scope
+                    break
+        except Exception:
+            self.h = None
+
+    def _read(self, scopes):
+        try:
+            ids = [(f, sc) for f in (self.FI_TX, self.FI_RX) for sc in scopes]
+            vals = self.nv.nvmlDeviceGetFieldValues(self.h, ids)
+        except Exception:
+            return None
+        tx = rx = 0
+        good = 0
+        for (f, _), v in zip(ids, vals):
+            if v.nvmlReturn != 0:
+                continue
+            good += 1
+            x = int(v.value.ullVal) * 1024
+            if f == self.FI_TX:
+                tx += x
+            else:
+                rx += x
+        return (tx, rx) if good else None
+
+    def read(self):
+        if self.h is None or self.scope is None:
+            return None
+        return self._read(self.scope)
 
 
 # ---------------------------------------------------------------------------------------------------------
@@ -369,6 +424,93 @@ def cpu_baseline(op, cfg, n, budget_s=20.0):
 
 
 # ---------------------------------------------------------------------------------------------------------
+# Parity of the timed collective (outside the timed region): its outputs against the C restatement of the
+# reference's algorithm (oracle/dt_oracle.c) on the same seeded inputs. Copies must be bit-exact; the
+# rank-order reductions bit-exact against the fp32-accumulate fold; the NVLS reduction (switch order) within
+# the north-star tolerance, allclose(rtol=2e-2, atol=2e-2 * rms) for bf16/fp16 and rtol 1e-6 for fp32.
+# ---------------------------------------------------------------------------------------------------------
+DT_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+RTOL = {torch.float32: 1e-6, torch.bfloat16: 2e-2, torch.float16: 2e-2}
+
+
+def raw_np(t):
+    """Raw storage of a tensor on the host: float32, or the uint16 bit patterns of bf16 / fp16."""
+    t = t.detach().contiguous().cpu()
+    return t.numpy() if t.dtype == torch.float32 else t.view(torch.int16).numpy().view(np.uint16)
+
+
+def raw_to_f32(a, code):
+    if code == 0:
+        return a.astype(np.float32)
+    if code == 1:
+        return (a.astype(np.uint32) << 16).view(np.float32)
+    return a.view(np.float16).astype(np.float32)
+
+
+class Parity:
+    """Accumulates output-vs-oracle comparisons into the line's `parity` object."""
+
+    def __init__(self, dtype, tolerance):
+        self.code = DT_CODE.get(dtype, 0)
+        self.rtol = RTOL.get(dtype, 0.0)
+        self.tolerance = tolerance  # False: bit-exact required
+        self.bit_exact = True
+        self.within = True
+        self.max_abs = 0.0
+        self.elements = 0
+        self.cases = 0
+
+    def compare(self, got, want):
+        got = np.asarray(got).reshape(-1)
+        want = np.asarray(want).reshape(-1)
+        self.cases += 1
+        self.elements += int(want.size)
+        if got.shape != want.shape:
+            self.bit_exact = self.within = False
+            self.max_abs = float("inf")
+            return
+        if np.array_equal(got, want):
+            return
+        self.bit_exact = False
+        g = raw_to_f32(got, self.code).astype(np.float64)
+        w = raw_to_f32(want, self.code).astype(np.float64)
+        err = np.abs(g - w)
+        self.max_abs = max(self.max_abs, float(np.nanmax(err)) if err.size else 0.0)
+        rms = float(np.sqrt(np.mean(w * w))) if w.size else 0.0
+        ok = bool(np.all(err <= self.rtol * rms + self.rtol * np.abs(w)))
+        self.within = self.within and ok and self.tolerance
+
+    @property
+    def ok(self):
+        return self.bit_exact or (self.tolerance and self.within)
+
+    def summary(self, what):
+        return {"checked": True, "ok": self.ok, "bit_exact": self.bit_exact, "max_abs_err": self.max_abs,
+                "elements": self.elements, "outputs": self.cases, "against": what,
+                "rule": ("within allclose(rtol, atol=rtol*rms), rtol=%g" % self.rtol) if self.tolerance
+                else "bit-exact"}
+
+
+def local_parity(w, par):
+    """Outputs of the same-device workload `w` against the restatement."""
+    from oracle.oracle import Restatement
+
+    R = Restatement()
+    host = [raw_np(t) for t in w.ins]
+    if w.op == "all_reduce":
+        want = [R.fold_sum(host, par.code, storage_round=False)]
+    elif w.op == "reduce_scatter":
+        want = R.reduce_scatter(host, par.code, storage_round=False)
+    elif w.op == "all_gather":
+        want = [R.all_gather(host, 0)]
+    else:
+        want = R.all_to_all(host, w.cfg["src_dim"], w.cfg["dst_dim"])
+    for got, wt in zip(w.outs, want):
+        par.compare(raw_np(got), wt)
+    return want
+
+
+# ---------------------------------------------------------------------------------------------------------
 # Arms
 # ---------------------------------------------------------------------------------------------------------
 def run_ours_single(args):
@@ -389,14 +531,22 @@ def run_ours_single(args):
         with torch.cuda.stream(stream):
             ms = time_steps(w.step, args.steps, stream)
     launches = capi.launch_count() - l0
+    # parity of what the timed steps wrote, against the restatement (outside the timed region)
+    par = Parity(cfg["dtype"], tolerance=False)
+    want = local_parity(w, par)
     # end to end: pinned host -> device, collective, device -> pinned host, every step
+    e2e_par = Parity(cfg["dtype"], tolerance=False)
     if args.skip_e2e:
         e2e_ms = float("nan")
     else:
+        for h in w.h_outs:
+            h.zero_()
         for _ in range(max(1, args.warmup // 2)):
             w.e2e_step()
         torch.cuda.synchronize()
         e2e_ms = time_steps(w.e2e_step, args.steps, stream)
+        for h, wt in zip(w.h_outs, want):
+            e2e_par.compare(raw_np(h), wt)
     t = ms / 1e3
     bus = w.msg_bytes * bus_factor(op, n) / t / 1e9
     e2e_bus = w.msg_bytes * bus_factor(op, n) / (e2e_ms / 1e3) / 1e9
@@ -440,8 +590,14 @@ def run_ours_single(args):
                          else "C ABI (dt_local_*) with pinned host buffers")},
         "gpu_launches": launches,
         "clocks": clk.summary(),
+        "parity": dict(par.summary("C restatement of the reference's fold / concat / split (oracle/dt_oracle.c), "
+                                   "fp32 accumulation in rank order; every output of the timed steps"),
+                       e2e_ok=e2e_par.ok if not args.skip_e2e else None),
     }
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
+    if not (par.ok and (args.skip_e2e or e2e_par.ok)):
+        print("parity check failed: the timed collective's output differs from the oracle", file=sys.stderr)
+        sys.exit(3)
 
 
 def run_reference(args, rank, world):
@@ -463,20 +619,50 @@ def run_reference(args, rank, world):
     t = statistics.median(secs[args.warmup:])
     msg = msg_bytes_of(op, ins)
     bus = msg * bus_factor(op, n) / t / 1e9
+    # same basis as our arm: at N > 1 the whole-job aggregate is the per-rank bus bandwidth times the ranks
+    value = bus * (n if world > 1 else 1)
     threads = cores if kind == "reference" else 1
     sample = (f"{'full workload' if frac >= 1 else f'{frac:.3f} of the workload (leading rows)'} per step, "
               f"n={n} rank threads, torch intra-op threads={threads}")
     line = {
-        "metric": "redistribute bus GB/s", "value": round(bus, 4), "unit": "GB/s", "n_gpus": world,
+        "metric": "redistribute bus GB/s", "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": DT_NAME[cfg["dtype"]],
         "data": "synthetic (seeded, BASELINE.json distribution)", "impl": "reference",
         "config": {"workload": cfg["name"] + f", reference CPU DeviceMesh path (ThreadGroupSameDeviceBackend), "
                    f"group of {n} rank threads", "op": op, "group_ranks": n, "msg_bytes_per_rank": msg},
-        "cpu_baseline": {"value": round(bus, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
-        "e2e": {"value": round(bus, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "bus_gbs_per_rank": round(bus, 4),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
+
+
+def multi_expected(op, cfg, n, rank, dev):
+    """This rank's expected output of the workload, from the restatement on the same seeded inputs (every rank
+    regenerates the inputs it needs on its own GPU, copies them to the host, and runs the C oracle)."""
+    from oracle.oracle import Restatement
+
+    R = Restatement()
+    dtype = cfg["dtype"]
+    code = DT_CODE[dtype]
+    if op == "all_reduce":
+        host = [raw_np(gen(cfg["shape"], dtype, r, cfg["dist"], dev).reshape(-1)) for r in range(n)]
+        return R.fold_sum(host, code, storage_round=False)
+    if op == "reduce_scatter":
+        numel = int(np.prod(cfg["shape"]))
+        lo, hi = numel // n * rank, numel // n * (rank + 1)
+        host = [raw_np(gen(cfg["shape"], dtype, r, cfg["dist"], dev).reshape(-1)[lo:hi]) for r in range(n)]
+        return R.fold_sum(host, code, storage_round=False)  # chunk `rank` of the fold = this rank's output
+    gs = cfg["global_shape"]
+    full = gen(gs, dtype, 0, cfg["dist"], dev)
+    if op == "all_gather":
+        shards = [raw_np(t) for t in torch.split(full, shard_sizes(gs[0], n), 0)]
+        return R.all_gather(shards, 0)
+    sd, dd = cfg["src_dim"], cfg["dst_dim"]
+    shards = [raw_np(t) for t in torch.split(full, shard_sizes(gs[sd], n), sd)]
+    del full
+    return R.all_to_all(shards, sd, dd, only=rank)[rank]
 
 
 def heap_tensor(base, offset, numel, dtype, device):
@@ -575,19 +761,33 @@ def run_ours_multi(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    nvl = NvLinkCounter(local_rank)
     l0 = capi.launch_count()
     with ClockSampler(local_rank) as clk:
         # ranks start their samplers at different times: line them up after, right before the timed steps
         dist.barrier()
         torch.cuda.synchronize()
+        c0 = nvl.read()
         ms = time_steps(step, args.steps, stream)
     launches = capi.launch_count() - l0
+    time.sleep(0.05)
+    c1 = nvl.read()
     dist.barrier()
     t_max = torch.tensor([ms], device=dev)
     dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms = float(t_max.item())
     err = comm.error(rank)
+    # NVLink payload bytes this GPU sent / received per launch (NVML counters around the timed steps)
+    nvl_tx = nvl_rx = None
+    if c0 is not None and c1 is not None:
+        nvl_tx = (c1[0] - c0[0]) / args.steps
+        nvl_rx = (c1[1] - c0[1]) / args.steps
+    # parity of the timed output against the restatement (every rank, outside the timed region)
+    want = multi_expected(op, cfg, n, rank, dev)
+    par = Parity(dtype, tolerance=(ar_flags == capi.DT_ALGO_NVLS))
+    par.compare(raw_np(y), want)
     p2p_bus = None
+    p2p_par = None
     if xp is not x:  # the rank-order P2P kernel on the same message, for comparison
         def pstep():
             comm.all_reduce(rank, xp.data_ptr(), yp.data_ptr(), in_numel, code, capi.DT_ALGO_TWOSHOT, stream.cuda_stream)
@@ -600,6 +800,13 @@ def run_ours_multi(args, rank, world, local_rank):
         t_max = torch.tensor([pms], device=dev)
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
         p2p_bus = msg * bus_factor(op, n) / (float(t_max.item()) / 1e3) / 1e9
+        p2p_par = Parity(dtype, tolerance=False)
+        p2p_par.compare(raw_np(yp), want)
+    # every rank's verdict, gathered on rank 0: [not ok, not bit-exact, max |err|, p2p leg not ok]
+    pv = torch.tensor([0.0 if par.ok else 1.0, 0.0 if par.bit_exact else 1.0, par.max_abs,
+                       0.0 if (p2p_par is None or p2p_par.ok) else 1.0], device=dev, dtype=torch.float64)
+    dist.all_reduce(pv, op=dist.ReduceOp.MAX)
+    del want
     # end to end: pinned host input -> heap, collective, heap output -> pinned host
     h_in = x.cpu().pin_memory()
     h_out = torch.empty(out_numel, dtype=dtype).pin_memory()
@@ -664,9 +871,22 @@ def run_ours_multi(args, rank, world, local_rank):
             "nccl_bus_gbs_per_rank": None if nccl_bus is None else round(nccl_bus, 2),
             "algorithm": algo,
             "p2p_bus_gbs_per_rank": None if p2p_bus is None else round(p2p_bus, 2),
-            "roofline": {"bound": "nvlink", "achieved": round(bus, 1), "peak": NVLINK_PEER_COPY_GBS, "unit": "GB/s",
-                         "frac": round(bus / NVLINK_PEER_COPY_GBS, 4), "traffic": None,
-                         "peak_source": "measured peer copy per direction (pool reference); nominal 900"},
+            "roofline": {"bound": "nvlink", "achieved": round(bus, 1), "peak": NVLINK_NOMINAL_GBS, "unit": "GB/s",
+                         "frac": round(bus / NVLINK_NOMINAL_GBS, 4),
+                         "traffic": None if nvl_tx is None else int(nvl_tx),
+                         "traffic_rx": None if nvl_rx is None else int(nvl_rx),
+                         "algorithmic_bytes_per_launch": int(msg * bus_factor(op, n)),
+                         "traffic_source": "NVML NVLink data counters (TX / RX payload bytes of rank 0's GPU) around "
+                                           "the timed steps, per launch",
+                         "peak_source": "NVLink 5 nominal, 900 GB/s per direction per GPU",
+                         "frac_of_p2p_ceiling": round(bus / NVLINK_P2P_CEILING_GBS, 4),
+                         "p2p_ceiling_source": "store ceiling measured both ways at once on one GPU pair "
+                                               "(profiles/nvlink_p2p_ceiling_probe.md)"},
+            "parity": {"checked": True, "ok": pv[0].item() == 0.0 and pv[3].item() == 0.0,
+                       "bit_exact": pv[1].item() == 0.0, "max_abs_err": float(pv[2].item()), "ranks": n,
+                       "rule": par.summary("")["rule"], "p2p_leg_ok": None if p2p_par is None else pv[3].item() == 0.0,
+                       "against": "C restatement of the reference's algorithm (oracle/dt_oracle.c), fp32 "
+                                  "accumulation in rank order, on every rank's full output"},
             "e2e": {"value": round(e2e_bus * n, 3), "unit": "GB/s", "h2d_bytes_per_step": in_numel * es,
                     "d2h_bytes_per_step": out_numel * es, "ms_per_step": round(e2e_ms, 4),
                     "path": "C ABI (dt_* on a multi-process dt_comm) with pinned host buffers"},
@@ -678,6 +898,10 @@ def run_ours_multi(args, rank, world, local_rank):
     dist.barrier()
     comm.destroy()
     dist.destroy_process_group()
+    if pv[0].item() != 0.0 or pv[3].item() != 0.0:
+        if rank == 0:
+            print("parity check failed: the timed collective's output differs from the oracle", file=sys.stderr)
+        sys.exit(3)
 
 
 # ---------------------------------------------------------------------------------------------------------

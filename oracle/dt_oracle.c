@@ -182,9 +182,13 @@ void oracle_all_gather(int n, const void* const* ins, void* out, size_t outer, c
     }
 }
 
-/* All-to-all (thread_group.cc:211-241), element by element: for destination rank k and each element of its
- * output, find the source rank i whose src-dim range holds the element's src coordinate, and read that rank's
- * input at the same coordinates except src (minus rank i's offset) and dst (plus chunk k's offset). */
+/* All-to-all (thread_group.cc:211-241): output k is the concatenation along src, in rank order, of chunk k
+ * (along dst, split with the shard rule) of every rank's input. Walked over the output's index space: for each
+ * output index, the source rank i is the one whose src-dim range holds the src coordinate, and the element is
+ * rank i's input at the same coordinates except src (minus rank i's offset) and dst (plus chunk k's offset).
+ * The dims after both src and dst are contiguous on both sides, so each index of the leading dims copies that
+ * whole trailing run at once. A NULL outs[k] skips destination k (a checker that holds one rank's output
+ * computes only that one). */
 void oracle_all_to_all(int n, const void* const* ins, void* const* outs, int ndim, const int64_t* in_shape,
                        int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_bytes) {
     int64_t split[8], doff[8], soff[8];
@@ -201,17 +205,22 @@ void oracle_all_to_all(int n, const void* const* ins, void* const* outs, int ndi
         acc += src_lens[r];
     }
     const int64_t A = acc;
+    const int lead = (src_dim > dst_dim ? src_dim : dst_dim) + 1; /* dims [0, lead) are walked */
+    int64_t run = 1;
+    for (int d = lead; d < ndim; ++d) run *= in_shape[d];
+    const size_t run_bytes = (size_t)run * elem_bytes;
     for (int k = 0; k < n; ++k) {
+        if (outs[k] == NULL) continue;
         int64_t oshape[16];
         for (int d = 0; d < ndim; ++d) oshape[d] = in_shape[d];
         oshape[src_dim] = A;
         oshape[dst_dim] = split[k];
         int64_t total = 1;
-        for (int d = 0; d < ndim; ++d) total *= oshape[d];
+        for (int d = 0; d < lead; ++d) total *= oshape[d];
         int64_t idx[16];
         for (int64_t e = 0; e < total; ++e) {
             int64_t rem = e;
-            for (int d = ndim - 1; d >= 0; --d) {
+            for (int d = lead - 1; d >= 0; --d) {
                 idx[d] = rem % oshape[d];
                 rem /= oshape[d];
             }
@@ -223,13 +232,13 @@ void oracle_all_to_all(int n, const void* const* ins, void* const* outs, int ndi
             for (int d = 0; d < ndim; ++d) ishape[d] = in_shape[d];
             ishape[src_dim] = src_lens[i];
             int64_t lin = 0;
-            for (int d = 0; d < ndim; ++d) {
+            for (int d = 0; d < lead; ++d) {
                 int64_t c = idx[d];
                 if (d == src_dim) c -= soff[i];
                 if (d == dst_dim) c += doff[k];
                 lin = lin * ishape[d] + c;
             }
-            memcpy((char*)outs[k] + (size_t)e * elem_bytes, (const char*)ins[i] + (size_t)lin * elem_bytes, elem_bytes);
+            memcpy((char*)outs[k] + (size_t)e * run_bytes, (const char*)ins[i] + (size_t)lin * run_bytes, run_bytes);
         }
     }
 }

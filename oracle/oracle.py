@@ -3,8 +3,8 @@
 Two checkers, both on the host:
 
 * ``Restatement`` wraps ``liboracle.so`` (dt_oracle.c): a plain-C restatement of what the reference's
-  same-device thread-group backend computes (thread_group_same_device_backend.cc:209-400,
-  thread_group.cc:209-323, distributed_spec.cc:202-213).
+  same-device thread-group backend computes (thread_group_same_device_backend.cc:111-302,
+  thread_group.cc:127-241, distributed_spec.cc:202-213).
 * ``Reference`` wraps ``_ref/libdtref.so``: the reference's own ThreadGroup / ThreadGroupSameDeviceBackend /
   MemoryTensorStore sources compiled out of tree (oracle/Makefile, target ``ref``), driven by n rank threads
   on a CPU DeviceMesh exactly as the reference drives them. It exists where the reference sources were
@@ -114,7 +114,9 @@ class Restatement:
         self.lib.oracle_all_gather(len(ins), _ptrs(ins), out.ctypes.data, outer, _i64(lens), inner)
         return out
 
-    def all_to_all(self, ins: Sequence[np.ndarray], src_dim: int, dst_dim: int) -> List[np.ndarray]:
+    def all_to_all(self, ins: Sequence[np.ndarray], src_dim: int, dst_dim: int,
+                   only: Optional[int] = None) -> List[Optional[np.ndarray]]:
+        """Every rank's output, or with ``only=k`` rank k's alone (the other entries are None)."""
         ins = [np.ascontiguousarray(a) for a in ins]
         n = len(ins)
         src_lens = [a.shape[src_dim] for a in ins]
@@ -122,6 +124,9 @@ class Restatement:
         split = shard_sizes(D, n)
         outs = []
         for k in range(n):
+            if only is not None and k != only:
+                outs.append(None)
+                continue
             shp = list(ins[0].shape)
             shp[src_dim] = sum(src_lens)
             shp[dst_dim] = split[k]

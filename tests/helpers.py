@@ -46,6 +46,35 @@ def assert_close(got: np.ndarray, ref: np.ndarray, dtype: str):
     assert not bad.any(), f"{int(bad.sum())} / {bad.size} elements outside rtol={rtol} atol={atol:g}"
 
 
+def abs_sum_f64(ins, dtype: str) -> np.ndarray:
+    """Per-element sum of |x_r| over the ranks' partials: the scale of the rounding error of any floating-point
+    summation of them (recursive summation of n terms errs by at most (n-1)·u·sum|x_r|, Higham, Accuracy and
+    Stability of Numerical Algorithms, section 4.2)."""
+    acc = np.zeros(ins[0].size, dtype=np.float64)
+    for a in ins:
+        acc += np.abs(to_f32(a.reshape(-1), dtype))
+    return acc
+
+
+def exact_sum_f64(ins, dtype: str) -> np.ndarray:
+    acc = np.zeros(ins[0].size, dtype=np.float64)
+    for a in ins:
+        acc += to_f32(a.reshape(-1), dtype)
+    return acc
+
+
+def assert_close_sum(got: np.ndarray, ref: np.ndarray, dtype: str, abs_sum: np.ndarray):
+    """|got - ref| <= rtol * sum_r |x_r| element by element: two summations of the same partials (here fp32
+    accumulation vs the reference's per-add rounding to bf16/fp16) agree to the error scale of summation itself.
+    At 64 M elements the rms-scaled form of assert_close flags the rare element where the reference's seven bf16
+    roundings drift on large partial sums that cancel; this scale follows the partial sums."""
+    g = to_f32(got.reshape(-1), dtype).astype(np.float64)
+    r = to_f32(ref.reshape(-1), dtype).astype(np.float64)
+    rtol = RTOL[dtype]
+    bad = np.abs(g - r) > rtol * abs_sum
+    assert not bad.any(), f"{int(bad.sum())} / {bad.size} elements outside rtol={rtol} of sum|x|"
+
+
 def torch_from_raw(a: np.ndarray, dtype: str, device="cpu"):
     import torch
 
