@@ -665,6 +665,104 @@ def multi_expected(op, cfg, n, rank, dev):
     return R.all_to_all(shards, sd, dd, only=rank)[rank]
 
 
+def run_api_leg(op, cfg, n, steps, warmup):
+    """The same collective through the reference-facing Python API in ONE process driving all n GPUs -- the
+    reference's single-controller model: DTensor.redistribute on a 1-D DeviceMesh, the C++ executor's
+    kernel-stream threads and ThreadGroup, locals and outputs in the group's symmetric pool. Device time = max
+    over the GPUs of CUDA events on each GPU's current stream around `steps` redistribute calls; parity of the
+    last result against the restatement."""
+    import dtorch_b200 as dtb
+    from oracle.oracle import Restatement
+
+    R = Restatement()
+    dtype = cfg["dtype"]
+    code = DT_CODE[dtype]
+    es = torch.tensor([], dtype=dtype).element_size()
+    devs = list(range(n))
+    mesh = dtb.DeviceMesh("cuda", devs)
+    if op in ("all_reduce", "reduce_scatter"):
+        shape = tuple(cfg["shape"])
+        msg = int(np.prod(shape)) * es
+        out_bytes = msg if op == "all_reduce" else msg // n
+    else:
+        shape = tuple(cfg["global_shape"])
+        msg = int(np.prod(shape)) * es if op == "all_gather" else int(np.prod(shape)) * es // n
+        out_bytes = int(np.prod(shape)) * es if op == "all_gather" else msg
+    # room for the input and several generations of outputs per GPU, so the host can run ahead of the GPUs
+    # while earlier outputs wait to be reclaimed
+    dtb.set_pool_bytes(((msg + 8 * out_bytes) >> 20) + 64 << 20)
+    dtb.clear()
+    try:
+        if op in ("all_reduce", "reduce_scatter"):
+            x = dtb.DTensor.empty({d: shape for d in devs}, dtype, mesh, [dtb.Partial()], shape)
+            host = []
+            for d in devs:
+                t = gen(shape, dtype, d, cfg["dist"], f"cuda:{d}")
+                x.local(d).copy_(t)
+                host.append(raw_np(t.reshape(-1)))
+            target = [dtb.Replicate()] if op == "all_reduce" else [dtb.Shard(0)]
+        else:
+            full = gen(shape, dtype, 0, cfg["dist"], "cuda:0").cpu()
+            src = [dtb.Shard(0)] if op == "all_gather" else [dtb.Shard(cfg["src_dim"])]
+            x = dtb.DTensor.from_torch(full, mesh, src)
+            target = [dtb.Replicate()] if op == "all_gather" else [dtb.Shard(cfg["dst_dim"])]
+        for d in devs:
+            torch.cuda.synchronize(d)
+        info = dtb.dtensor._host.pool_info(devs, 0)
+        in_pool = all(dtb.dtensor._host.in_pool(devs, d, x.local(d)) for d in devs)
+        y = None
+        for _ in range(warmup):
+            y = x.redistribute(placements=target)
+        for d in devs:
+            torch.cuda.synchronize(d)
+        ev = {d: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for d in devs}
+        for d in devs:
+            ev[d][0].record(torch.cuda.current_stream(d))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            y = x.redistribute(placements=target)
+        host_s = (time.perf_counter() - t0) / steps
+        for d in devs:
+            ev[d][1].record(torch.cuda.current_stream(d))
+        for d in devs:
+            torch.cuda.synchronize(d)
+        ms = max(ev[d][0].elapsed_time(ev[d][1]) for d in devs) / steps
+        out_in_pool = all(dtb.dtensor._host.in_pool(devs, d, y.local(d)) for d in devs)
+        nvls = bool(info["nvls"]) and op == "all_reduce" and n >= 4 and msg >= (16 << 20 if n < 6 else 8 << 20)
+        par = Parity(dtype, tolerance=nvls)
+        if op == "all_reduce":
+            want = R.fold_sum(host, code, storage_round=False)
+            for d in devs:
+                par.compare(raw_np(y.local(d)), want)
+        elif op == "reduce_scatter":
+            rows = shape[0] // n
+            want = R.reduce_scatter([h.reshape(shape) for h in host], code, storage_round=False)
+            for d in devs:
+                par.compare(raw_np(y.local(d)), want[d].reshape(rows, *shape[1:]))
+        elif op == "all_gather":
+            par.compare(raw_np(y.local(0)), raw_np(full))
+            for d in devs[1:]:
+                par.compare(raw_np(y.local(d)), raw_np(full))
+        else:
+            sd, dd = cfg["src_dim"], cfg["dst_dim"]
+            shards = [raw_np(t) for t in torch.split(full, shard_sizes(shape[sd], n), sd)]
+            want = R.all_to_all(shards, sd, dd)
+            for d in devs:
+                par.compare(raw_np(y.local(d)), want[d])
+        bus = msg * bus_factor(op, n) / (ms / 1e3) / 1e9
+        return {"bus_gbs_per_rank": round(bus, 2), "value": round(bus * n, 2), "ms_per_step": round(ms, 5),
+                "host_ms_per_call": round(host_s * 1e3, 4),
+                "path": "one process, DTensor.redistribute on DeviceMesh('cuda', range(n)) -> C++ executor -> "
+                        "ThreadGroup -> C ABI; locals and outputs in the group's symmetric pool",
+                "pool": {"bytes": int(info["bytes"]), "nvls": bool(info["nvls"]), "inputs_in_pool": in_pool,
+                         "outputs_in_pool": out_in_pool},
+                "algorithm": "nvls (in-switch reduction)" if nvls else "rank-order P2P kernels",
+                "parity": par.summary("C restatement (oracle/dt_oracle.c) on every GPU's output")}
+    finally:
+        dtb.clear()
+        dtb.set_pool_bytes(0)
+
+
 def heap_tensor(base, offset, numel, dtype, device):
     from dtorch_b200.multiprocess import device_view
 
@@ -686,6 +784,9 @@ def run_ours_multi(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
+    # host-only group: the other ranks wait on it while rank 0 drives every GPU in the API leg, so no NCCL
+    # kernel sits on their GPUs meanwhile
+    cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
     dtype = cfg["dtype"]
     es = torch.tensor([], dtype=dtype).element_size()
     # per-rank buffers
@@ -849,6 +950,20 @@ def run_ours_multi(args, rank, world, local_rank):
         nccl_bus = msg * bus_factor(op, n) / (float(t_max.item()) / 1e3) / 1e9
     bus = msg * bus_factor(op, n) / (ms / 1e3) / 1e9
     e2e_bus = msg * bus_factor(op, n) / (e2e_ms / 1e3) / 1e9
+    # free this process's communicator before rank 0 drives every GPU from one process
+    del x, y, xp, yp
+    torch.cuda.synchronize()
+    dist.barrier()
+    comm.destroy()
+    torch.cuda.synchronize()
+    dist.barrier(group=cpu_group)
+    api = None
+    if rank == 0 and not args.skip_api:
+        try:
+            api = run_api_leg(op, cfg, n, args.steps, args.warmup)
+        except Exception as e:  # reported in the line; the C-ABI figures above stand on their own
+            api = {"error": repr(e)[:400]}
+    dist.barrier(group=cpu_group)
     if rank == 0:
         line = {
             "metric": "redistribute bus GB/s",
@@ -893,12 +1008,13 @@ def run_ours_multi(args, rank, world, local_rank):
             "gpu_launches": launches,
             "device_error": err,
             "clocks": clk.summary(),
+            "api": api,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
-    comm.destroy()
     dist.destroy_process_group()
-    if pv[0].item() != 0.0 or pv[3].item() != 0.0:
+    api_bad = rank == 0 and isinstance(api, dict) and "parity" in api and not api["parity"]["ok"]
+    if pv[0].item() != 0.0 or pv[3].item() != 0.0 or api_bad:
         if rank == 0:
             print("parity check failed: the timed collective's output differs from the oracle", file=sys.stderr)
         sys.exit(3)
@@ -1107,6 +1223,7 @@ def main():
     p.add_argument("--op", choices=list(CONFIGS), default="all_reduce")
     p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline (profiling runs)")
     p.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end leg (profiling runs)")
+    p.add_argument("--skip-api", action="store_true", help="N > 1: omit the single-process DTensor API leg")
     p.add_argument("--algo", choices=["auto", "p2p", "nvls"], default="auto",
                    help="all-reduce algorithm at N > 1: auto = NVLS where supported and n >= 4, else P2P two-shot")
     p.add_argument("--sweep", action="store_true", help="C5 message-size sweep, one JSON line per point")

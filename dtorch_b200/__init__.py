@@ -12,7 +12,7 @@ __version__ = "0.1.0"
 
 _DTENSOR_NAMES = ("DeviceMesh", "Placement", "Shard", "Replicate", "Partial", "init_device_mesh", "DTensor",
                   "get_placements_from_dict",
-                  "cuda_device_of", "clear", "redistribute_many", "reduce")
+                  "cuda_device_of", "clear", "redistribute_many", "reduce", "set_pool_bytes")
 
 
 def __getattr__(name):

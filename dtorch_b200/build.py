@@ -53,7 +53,7 @@ def build_capi(force: bool = False, verbose: bool = False) -> str:
     return out
 
 
-HOST_SRCS = ["placement.cpp", "thread_group.cpp", "redistribute.cpp", "bindings.cpp"]
+HOST_SRCS = ["placement.cpp", "sym_pool.cpp", "thread_group.cpp", "redistribute.cpp", "bindings.cpp"]
 
 
 def build_host(force: bool = False, verbose: bool = False) -> str:

@@ -73,6 +73,8 @@ SIGNATURES = [
     ("dt_comm_nvls_bind", _I, [_P]),
     ("dt_comm_nvls_buffer", _I, [_P, _I, _P, _P]),
     ("dt_local_all_reduce_host_noalloc", _I, [_I, _P, _P, _SZ, _I, _I, _P]),
+    ("dt_all_to_all_list", _I, [_P, _I, _P, _P, _P, _P, _P]),
+    ("dt_all_gather_list", _I, [_P, _I, _P, _SZ, _P, _P, _P]),
 ]
 
 
@@ -124,6 +126,10 @@ def ptr_array(ptrs: Sequence[int]):
     for i, p in enumerate(ptrs):
         arr[i] = p
     return arr
+
+
+def size_array(vals: Sequence[int]):
+    return (ctypes.c_size_t * len(vals))(*[int(v) for v in vals])
 
 
 def i64_array(vals: Sequence[int]):
@@ -250,6 +256,14 @@ class Comm:
         check(lib().dt_all_to_all_multi(self._h, rank, len(ins), ptr_array(ins), ptr_array(outs), len(in_shape),
                                         i64_array(in_shape), src_dim, dst_dim, i64_array(src_lens), elem_bytes, stream),
               "dt_all_to_all_multi")
+
+    def all_to_all_list(self, rank, ins, in_bytes, outs, out_bytes, stream=0):
+        check(lib().dt_all_to_all_list(self._h, rank, ptr_array(ins), size_array(in_bytes), ptr_array(outs),
+                                       size_array(out_bytes), stream), "dt_all_to_all_list")
+
+    def all_gather_list(self, rank, inp, in_bytes, outs, out_bytes, stream=0):
+        check(lib().dt_all_gather_list(self._h, rank, inp, in_bytes, ptr_array(outs), size_array(out_bytes), stream),
+              "dt_all_gather_list")
 
     def barrier(self, rank, stream=0):
         check(lib().dt_barrier(self._h, rank, stream), "dt_barrier")

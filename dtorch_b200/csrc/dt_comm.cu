@@ -113,6 +113,11 @@ struct Slot {
     void* out;
     cudaStream_t stream;
     void* extra[kMaxRanks];  // further outputs of a multi-tensor call, copied by value
+    // list forms (one buffer per peer): inputs, outputs and byte counts of the publishing rank
+    const void* lin[kMaxRanks];
+    void* lout[kMaxRanks];
+    size_t lbytes[kMaxRanks];  // bytes sent to rank k
+    size_t lcap[kMaxRanks];    // room in lout[k] for what rank k sends
 };
 
 }  // namespace
@@ -249,20 +254,34 @@ bool in_heap(const dt_comm* c, int rank, const void* p, size_t bytes) {
     return q >= s.heap && q + bytes <= s.heap + c->heap_bytes;
 }
 
-// Resolve every rank's in/out pointer as addressed from `rank`'s device: symmetric-heap offsets when both
-// buffers live in the heap, otherwise (single process only) the per-call rendezvous.
+// Every rank's copy of a buffer that sits at the same offset of symmetric memory on every rank, as addressed
+// from `rank`'s device: the symmetric heap (both modes), or the NVLS buffer's unicast mappings (single process,
+// where every rank's mapping is open to every device). False if `p` is in neither.
+bool symmetric_peers(const dt_comm* c, int rank, const void* p, size_t bytes, const char** peers) {
+    const RankState& s = c->r[rank];
+    const char* q = static_cast<const char*>(p);
+    if (bytes == 0) {
+        for (int r = 0; r < c->n; ++r) peers[r] = q;
+        return true;
+    }
+    if (in_heap(c, rank, p, bytes)) {
+        for (int r = 0; r < c->n; ++r) peers[r] = s.peer_heap[r] + (q - s.heap);
+        return true;
+    }
+    if (!c->multiprocess && s.nvls_uc != nullptr && q >= s.nvls_uc && q + bytes <= s.nvls_uc + c->nvls_size) {
+        for (int r = 0; r < c->n; ++r) peers[r] = c->r[r].nvls_uc + (q - s.nvls_uc);
+        return true;
+    }
+    return false;
+}
+
+// Resolve every rank's in/out pointer as addressed from `rank`'s device: symmetric offsets when both buffers
+// live in symmetric memory (heap or NVLS buffer), otherwise (single process only) the per-call rendezvous.
 int resolve_peers(dt_comm* c, int rank, const void* in, size_t in_bytes, void* out, size_t out_bytes,
                   const char** ins, char** outs) {
-    RankState& s = c->r[rank];
-    const bool heap_in = in_bytes == 0 || in_heap(c, rank, in, in_bytes);
-    const bool heap_out = out_bytes == 0 || in_heap(c, rank, out, out_bytes);
-    if (heap_in && heap_out) {
-        const ptrdiff_t oi = static_cast<const char*>(in) - s.heap;
-        const ptrdiff_t oo = static_cast<char*>(out) - s.heap;
-        for (int r = 0; r < c->n; ++r) {
-            ins[r] = s.peer_heap[r] + oi;
-            outs[r] = s.peer_heap[r] + oo;
-        }
+    const char* sym_out[kMaxRanks];
+    if (symmetric_peers(c, rank, in, in_bytes, ins) && symmetric_peers(c, rank, out, out_bytes, sym_out)) {
+        for (int r = 0; r < c->n; ++r) outs[r] = const_cast<char*>(sym_out[r]);
         return DT_OK;
     }
     if (c->multiprocess) {
@@ -443,18 +462,32 @@ int64_t copy_want_blocks(int64_t max_row_bytes, int64_t rows, int nseg) {
     return std::max<int64_t>(1, (items * nseg + warps - 1) / warps);
 }
 
-template <int VW, int MAXSEG, bool BAR>
-int launch_copy_t(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks) {
-    constexpr int SEGB = CopyGeom<VW>::kSegBytes;
+template <int VW>
+void set_geom(Seg& s) {
+    s.vw = VW;
+    s.seg_bytes = CopyGeom<VW>::kSegBytes;
+}
+
+// Per segment: merge contiguous row dims, pick the widest access its pointers, strides and run allow, and
+// count its pieces. Then one launch for the whole set.
+template <int MAXSEG, bool BAR>
+int launch_copy(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks = 0) {
     a.max_items = 0;
     for (int i = 0; i < a.nseg; ++i) {
         Seg& s = a.seg[i];
+        finish_seg(s, 0);
+        const uint64_t g = s.run > 0 ? seg_align(s) : 16;
+        if (g % 16 == 0) set_geom<16>(s);
+        else if (g % 8 == 0) set_geom<8>(s);
+        else if (g % 4 == 0) set_geom<4>(s);
+        else if (g % 2 == 0) set_geom<2>(s);
+        else set_geom<1>(s);
         const int64_t rows = s.cnt[0] * s.cnt[1] * s.cnt[2];
-        s.spr = s.run > 0 ? (s.run + SEGB - 1) / SEGB : 0;
+        s.spr = s.run > 0 ? (s.run + s.seg_bytes - 1) / s.seg_bytes : 0;
         s.items = rows * s.spr;
         a.max_items = std::max(a.max_items, s.items);
     }
-    auto k = k_copy<VW, MAXSEG, BAR>;
+    auto k = k_copy<MAXSEG, BAR>;
     int per_sm = kCopyBlocksPerSM;
     if (BAR && want_blocks > 0) {
         // peer copies, measured at 8 GPUs: one CTA per SM keeps the fabric less congested up to ~256 MiB
@@ -470,20 +503,6 @@ int launch_copy_t(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream
     pick_grid(k, dev, num_sms, want_blocks, per_sm, &grid);
     k<<<grid, kThreads, 0, stream>>>(a);
     return launch_check("k_copy");
-}
-
-template <int MAXSEG, bool BAR>
-int launch_copy(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream, int64_t want_blocks = 0) {
-    uint64_t g = 16;
-    for (int i = 0; i < a.nseg; ++i) {
-        finish_seg(a.seg[i], 0);
-        if (a.seg[i].run > 0) g = gcd_u64(g, seg_align(a.seg[i]));
-    }
-    if (g % 16 == 0) return launch_copy_t<16, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
-    if (g % 8 == 0) return launch_copy_t<8, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
-    if (g % 4 == 0) return launch_copy_t<4, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
-    if (g % 2 == 0) return launch_copy_t<2, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
-    return launch_copy_t<1, MAXSEG, BAR>(a, dev, num_sms, stream, want_blocks);
 }
 
 // Shard sizes: the first L % n ranks get one more (Placement::GetShardSizeForAllRank,
@@ -576,13 +595,14 @@ int a2a_geom(int n, int ndim, const int64_t* in_shape, int src_dim, int dst_dim,
 // call (its `ready` event); the others chain their streams on `done`. `body` issues the kernel on rank 0's
 // stream given every rank's Slot.
 template <typename Body>
-int same_device_call(dt_comm* c, int rank, const void* in, void* out, cudaStream_t stream, Body body) {
+int same_device_call(dt_comm* c, int rank, Slot mine, cudaStream_t stream, Body body) {
     RankState& s = c->r[rank];
     DT_CUDA(cudaSetDevice(s.dev));
     DT_CUDA(cudaEventRecord(s.ready, stream));
     const uint64_t my_gen = s.rv_gen;
     Slot all[kMaxRanks];
-    int st = rendezvous(c, rank, Slot{in, out, stream}, all);
+    mine.stream = stream;
+    int st = rendezvous(c, rank, mine, all);
     if (st != DT_OK) return st;
     if (rank == 0) {
         int rc = DT_OK;
@@ -611,6 +631,14 @@ int same_device_call(dt_comm* c, int rank, const void* in, void* out, cudaStream
     if (rc != DT_OK) return fail(rc, "same-device: rank 0 failed to launch the collective");
     DT_CUDA(cudaStreamWaitEvent(stream, c->done, 0));
     return DT_OK;
+}
+
+template <typename Body>
+int same_device_call(dt_comm* c, int rank, const void* in, void* out, cudaStream_t stream, Body body) {
+    Slot mine{};
+    mine.in = in;
+    mine.out = out;
+    return same_device_call(c, rank, mine, stream, body);
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -1452,14 +1480,14 @@ int dt_all_to_all_multi(dt_comm* c, int rank, int ntensors, const void* const* i
     DT_CUDA(cudaSetDevice(s.dev));
     // every rank's output pointers of every tensor, as addressed from this device
     char* outs[kMaxRanks][kMaxRanks];  // [tensor][rank]
-    bool heap = true;
-    for (int t = 0; t < ntensors; ++t)
-        heap = heap && in_heap(c, rank, outs_v[t], static_cast<size_t>(out_elems) * elem_b);
-    if (heap) {
-        for (int t = 0; t < ntensors; ++t) {
-            const ptrdiff_t o = static_cast<char*>(outs_v[t]) - s.heap;
-            for (int r = 0; r < c->n; ++r) outs[t][r] = s.peer_heap[r] + o;
-        }
+    bool sym = true;
+    for (int t = 0; t < ntensors && sym; ++t) {
+        const char* peers[kMaxRanks];
+        sym = symmetric_peers(c, rank, outs_v[t], static_cast<size_t>(out_elems) * elem_b, peers);
+        for (int r = 0; sym && r < c->n; ++r) outs[t][r] = const_cast<char*>(peers[r]);
+    }
+    if (sym) {
+        // every output is in symmetric memory: nothing to exchange
     } else if (c->multiprocess) {
         return fail(DT_ERR_INVALID, "multi-process communicator: buffers must live in the symmetric heap");
     } else {
@@ -1490,6 +1518,129 @@ int dt_all_to_all_multi(dt_comm* c, int rank, int ntensors, const void* const* i
     const int64_t rows = g.d0 * g.dmid * (g.src_first ? max_l : max_k);
     const int64_t want = copy_want_blocks(run, rows, c->n * ntensors);
     return launch_copy<kMaxRanks * kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+}
+
+// ---- list forms (c10d's allgather / alltoall with one tensor per rank) ------------------------------------
+
+}  // extern "C"
+
+namespace {
+
+// Launch one segment per (source, destination) pair: rank i's ins[k] -> rank k's outs[i], `bytes[i][k]`.
+// Peer mode: this rank's row only, every rank the same grid (sized from every rank's sizes).
+int list_copy(dt_comm* c, int rank, const Slot* all, cudaStream_t stream, bool same_device) {
+    RankState& s = c->r[rank];
+    int64_t max_bytes = 0;
+    for (int i = 0; i < c->n; ++i)
+        for (int k = 0; k < c->n; ++k) max_bytes = std::max<int64_t>(max_bytes, static_cast<int64_t>(all[i].lbytes[k]));
+    if (same_device) {
+        CopyArgs<kMaxRanks * kMaxRanks> a{};
+        a.nseg = c->n * c->n;
+        for (int j = 0; j < c->n; ++j)
+            for (int i = 0; i < c->n; ++i) {
+                const int k = (i + j) % c->n;
+                Seg& g = a.seg[j * c->n + i];
+                g = Seg{};
+                g.src = static_cast<const char*>(all[i].lin[k]);
+                g.dst = static_cast<char*>(all[k].lout[i]);
+                g.run = static_cast<int64_t>(all[i].lbytes[k]);
+                g.cnt[0] = g.cnt[1] = g.cnt[2] = 1;
+            }
+        return launch_copy<kMaxRanks * kMaxRanks, false>(a, s.dev, s.num_sms, stream);
+    }
+    CopyArgs<kMaxRanks> a{};
+    a.sig = make_sig(c, rank);
+    a.nseg = c->n;
+    for (int j = 0; j < c->n; ++j) {
+        const int k = (rank + 1 + j) % c->n;  // destinations in rotated order, own copy last
+        Seg& g = a.seg[j];
+        g = Seg{};
+        g.src = static_cast<const char*>(all[rank].lin[k]);
+        g.dst = static_cast<char*>(all[k].lout[rank]);
+        g.run = static_cast<int64_t>(all[rank].lbytes[k]);
+        g.cnt[0] = g.cnt[1] = g.cnt[2] = 1;
+    }
+    const int64_t want = copy_want_blocks(max_bytes, 1, c->n);
+    return launch_copy<kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+}
+
+// Arguments of every rank, checked together so that every rank reaches the same verdict (a rank that launched
+// alone would wait for its peers until the timeout): buffers present, and what rank i sends to rank k fits
+// the room rank k gave for it.
+int list_check(const dt_comm* c, const Slot* all, const char* what) {
+    for (int i = 0; i < c->n; ++i)
+        for (int k = 0; k < c->n; ++k) {
+            if ((all[i].lbytes[k] > 0 && all[i].lin[k] == nullptr) || (all[k].lcap[i] > 0 && all[k].lout[i] == nullptr))
+                return fail(DT_ERR_INVALID, std::string(what) + ": null buffer");
+            if (all[i].lbytes[k] > all[k].lcap[i])
+                return fail(DT_ERR_INVALID, std::string(what) + ": rank " + std::to_string(i) + " sends " +
+                                                std::to_string(all[i].lbytes[k]) + " bytes to rank " +
+                                                std::to_string(k) + ", which has room for " +
+                                                std::to_string(all[k].lcap[i]));
+        }
+    return DT_OK;
+}
+
+int list_call(dt_comm* c, int rank, const Slot& mine, void* stream_v, const char* what) {
+    int st = common_checks(c, rank);
+    if (st != DT_OK) return st;
+    if (c->multiprocess)
+        return fail(DT_ERR_UNSUPPORTED, std::string(what) + ": the list forms exchange buffer lists in process; "
+                                        "use a single-process communicator");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+    RankState& s = c->r[rank];
+    if (c->same_device) {
+        return same_device_call(c, rank, mine, stream, [&](const Slot* all, cudaStream_t st0) -> int {
+            const int rc = list_check(c, all, what);
+            return rc != DT_OK ? rc : list_copy(c, rank, all, st0, true);
+        });
+    }
+    DT_CUDA(cudaSetDevice(s.dev));
+    Slot all[kMaxRanks];
+    st = rendezvous(c, rank, mine, all);
+    if (st != DT_OK) return st;
+    st = list_check(c, all, what);
+    if (st != DT_OK) return st;
+    if (c->n == 1) {
+        if (mine.lbytes[0] > 0 && mine.lin[0] != mine.lout[0])
+            DT_CUDA(cudaMemcpyAsync(mine.lout[0], mine.lin[0], mine.lbytes[0], cudaMemcpyDeviceToDevice, stream));
+        return DT_OK;
+    }
+    return list_copy(c, rank, all, stream, false);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dt_all_to_all_list(dt_comm* c, int rank, const void* const* ins, const size_t* in_bytes, void* const* outs,
+                       const size_t* out_bytes, void* stream) {
+    DeviceGuard device_guard;
+    if (c == nullptr || ins == nullptr || outs == nullptr || in_bytes == nullptr || out_bytes == nullptr)
+        return fail(DT_ERR_INVALID, "dt_all_to_all_list: null argument");
+    Slot mine{};
+    for (int k = 0; k < c->n && k < kMaxRanks; ++k) {
+        mine.lin[k] = ins[k];
+        mine.lbytes[k] = in_bytes[k];
+        mine.lout[k] = outs[k];
+        mine.lcap[k] = out_bytes[k];
+    }
+    return list_call(c, rank, mine, stream, "dt_all_to_all_list");
+}
+
+int dt_all_gather_list(dt_comm* c, int rank, const void* in, size_t in_bytes, void* const* outs,
+                       const size_t* out_bytes, void* stream) {
+    DeviceGuard device_guard;
+    if (c == nullptr || outs == nullptr || out_bytes == nullptr)
+        return fail(DT_ERR_INVALID, "dt_all_gather_list: null argument");
+    Slot mine{};
+    for (int k = 0; k < c->n && k < kMaxRanks; ++k) {
+        mine.lin[k] = in;  // the same input goes to every rank
+        mine.lbytes[k] = in_bytes;
+        mine.lout[k] = outs[k];
+        mine.lcap[k] = out_bytes[k];
+    }
+    return list_call(c, rank, mine, stream, "dt_all_gather_list");
 }
 
 int dt_barrier(dt_comm* c, int rank, void* stream_v) {

@@ -287,8 +287,10 @@ __global__ void __launch_bounds__(kThreads) k_reduce(const __grid_constant__ Red
 // with independent source and destination byte strides. All-gather along any dim and the all-to-all pack
 // and concat are all such sets: the strided read of the shard-dim slice and the placement at the concat
 // offset happen inside the copy, so no separate contiguous() or concat pass touches HBM.
-// Work item = one segment of up to kSegBytes of one row, copied by one warp (16-byte vectors when VW = 16).
-// Items of different destinations are interleaved so every peer link is busy at once.
+// Work item = one piece of up to seg_bytes of one row, copied by one warp with the segment's own access
+// width (16-byte vectors when its pointers, strides and run allow, narrower otherwise -- one odd segment
+// does not slow the others down). Items of different destinations are interleaved so every peer link is
+// busy at once.
 // ------------------------------------------------------------------------------------------------------------
 struct Seg {
     const char* src;
@@ -297,8 +299,10 @@ struct Seg {
     int64_t cnt[3];    // row index extents (i0, i1, i2)
     int64_t ss[3];     // source byte strides
     int64_t ds[3];     // destination byte strides
-    int64_t spr;       // segments per row
+    int64_t spr;       // pieces per row
     int64_t items;     // rows * spr
+    int32_t vw;        // access width in bytes: 16, 8, 4, 2 or 1
+    int32_t seg_bytes; // bytes per piece (CopyGeom<vw>::kSegBytes)
 };
 
 template <int MAXSEG>
@@ -328,11 +332,48 @@ struct CopyGeom {
     static constexpr int kSegBytes = 32 * VW * kU;    // bytes per item
 };
 
-template <int VW, int MAXSEG, bool BARRIER>
-__global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyArgs<MAXSEG> a) {
+// One piece (`len` bytes at src -> dst) copied by one warp with VW-byte accesses: all loads first, then all
+// stores, so each lane has kU independent accesses in flight.
+template <int VW>
+__device__ __forceinline__ void copy_piece(const char* src, char* dst, int64_t len, int lane) {
     using V = typename VecOf<VW>::T;
     constexpr int U = CopyGeom<VW>::kU;
-    constexpr int SEG = CopyGeom<VW>::kSegBytes;
+    const V* s = reinterpret_cast<const V*>(src);
+    V* d = reinterpret_cast<V*>(dst);
+    V buf[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t off = static_cast<int64_t>(u * 32 + lane) * VW;
+        if (off < len) buf[u] = s[u * 32 + lane];
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t off = static_cast<int64_t>(u * 32 + lane) * VW;
+        if (off < len) d[u * 32 + lane] = buf[u];
+    }
+}
+
+// Pieces of segments whose pointers, strides or run are not 16-byte multiples: the same work with 8-, 4-, 2- or
+// 1-byte accesses, a plain strided loop per lane. Kept out of line and lean so that it does not weigh on the
+// registers of the 16-byte path around it; such segments are the exception (odd shard extents).
+template <typename V>
+__device__ __forceinline__ void copy_strided(const char* src, char* dst, int64_t len, int lane) {
+    constexpr int64_t W = sizeof(V);
+    for (int64_t o = lane * W; o < len; o += 32 * W)
+        *reinterpret_cast<V*>(dst + o) = *reinterpret_cast<const V*>(src + o);
+}
+
+__device__ __noinline__ void copy_piece_narrow(const char* src, char* dst, int64_t len, int lane, int vw) {
+    switch (vw) {
+        case 8: copy_strided<uint2>(src, dst, len, lane); break;
+        case 4: copy_strided<uint32_t>(src, dst, len, lane); break;
+        case 2: copy_strided<uint16_t>(src, dst, len, lane); break;
+        default: copy_strided<uint8_t>(src, dst, len, lane); break;
+    }
+}
+
+template <int MAXSEG, bool BARRIER>
+__global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyArgs<MAXSEG> a) {
     uint32_t e = 0;
     if (BARRIER) {
         e = block_epoch(a.sig);
@@ -352,7 +393,7 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyA
             row = j / s.spr;
             sg = j - row * s.spr;
         }
-        int64_t so = sg * SEG, dof = sg * SEG;
+        int64_t so = sg * s.seg_bytes, dof = sg * s.seg_bytes;
         if (s.cnt[0] == 1 && s.cnt[1] == 1) {
             so += row * s.ss[2];
             dof += row * s.ds[2];
@@ -364,19 +405,11 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyA
             so += i0 * s.ss[0] + i1 * s.ss[1] + i2 * s.ss[2];
             dof += i0 * s.ds[0] + i1 * s.ds[1] + i2 * s.ds[2];
         }
-        const int64_t len = min(static_cast<int64_t>(SEG), s.run - sg * SEG);
-        const V* src = reinterpret_cast<const V*>(s.src + so);
-        V* dst = reinterpret_cast<V*>(s.dst + dof);
-        V buf[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t off = static_cast<int64_t>(u * 32 + lane) * VW;
-            if (off < len) buf[u] = src[u * 32 + lane];
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t off = static_cast<int64_t>(u * 32 + lane) * VW;
-            if (off < len) dst[u * 32 + lane] = buf[u];
+        const int64_t len = min(static_cast<int64_t>(s.seg_bytes), s.run - sg * s.seg_bytes);
+        if (s.vw == 16) {
+            copy_piece<16>(s.src + so, s.dst + dof, len, lane);
+        } else {
+            copy_piece_narrow(s.src + so, s.dst + dof, len, lane, s.vw);
         }
     }
     if (BARRIER) block_barrier(a.sig, 2 * e);

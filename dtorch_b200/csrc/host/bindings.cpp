@@ -75,6 +75,35 @@ PYBIND11_MODULE(_host, m) {
           },
           py::return_value_policy::reference, py::call_guard<py::gil_scoped_release>(),
           "ThreadGroup of the group `ids` for the rank on device `current` (created on first use)");
+    m.def("set_pool_bytes", &SetPoolBytes, py::arg("bytes"),
+          "bytes of symmetric pool (NVLS buffer or symmetric heap) each peer-mode group created from now on gets");
+    m.def("pool_bytes", &PoolBytes);
+    m.def("pool_empty",
+          [](const std::vector<int64_t>& ids, int64_t current, const std::vector<int64_t>& shape, py::object dtype,
+             size_t bytesAllRanks) {
+              const auto st = torch::python::detail::py_object_to_dtype(dtype);
+              py::gil_scoped_release nogil;
+              ThreadGroup& tg = ThreadGroupManager::Global().GetThreadGroup(ids, current);
+              auto opts = torch::TensorOptions().dtype(st).device(torch::kCUDA, CudaDeviceOf(current));
+              return tg.NewOutput(shape, opts, bytesAllRanks);
+          },
+          "a tensor for device `current` from the symmetric pool of the group `ids` (torch.empty when the group has "
+          "no pool or it is full); every device of the group must make the same sequence of these calls with the "
+          "same bytes_all_ranks");
+    m.def("pool_info", [](const std::vector<int64_t>& ids, int64_t current) {
+        ThreadGroup& tg = ThreadGroupManager::Global().GetThreadGroup(ids, current);
+        py::dict d;
+        SymmetricPool* p = tg.Pool();
+        d["bytes"] = p ? p->bytes() : 0;
+        d["nvls"] = p ? p->nvls() : false;
+        d["in_use"] = p ? p->InUse() : 0;
+        return d;
+    });
+    m.def("in_pool", [](const std::vector<int64_t>& ids, int64_t current, const torch::Tensor& t) {
+        ThreadGroup& tg = ThreadGroupManager::Global().GetThreadGroup(ids, current);
+        SymmetricPool* p = tg.Pool();
+        return p != nullptr && t.defined() && p->Owns(tg.GetRank(), t.data_ptr());
+    });
     m.def("clear", []() {
         KernelStreamManager::Global().Clear();
         ThreadGroupManager::Global().Clear();

@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <numeric>
 #include <stdexcept>
@@ -66,13 +67,53 @@ int DTypeCode(at::ScalarType t) {
     }
 }
 
-SharedComm::SharedComm(const std::vector<int>& cudaDevices) : mDevices(cudaDevices) {
-    Check(dt_comm_create(static_cast<int>(cudaDevices.size()), cudaDevices.data(), 0, &mComm), "dt_comm_create");
+namespace {
+std::atomic<int64_t> gPoolBytesOverride{-1};
+}  // namespace
+
+size_t PoolBytes() {
+    const int64_t o = gPoolBytesOverride.load();
+    if (o >= 0) return static_cast<size_t>(o);
+    const char* s = std::getenv("DTORCH_B200_POOL_MB");
+    if (s == nullptr || *s == '\0') return 0;
+    const long long mb = std::atoll(s);
+    return mb > 0 ? static_cast<size_t>(mb) << 20 : 0;
+}
+
+void SetPoolBytes(size_t bytes) { gPoolBytesOverride.store(static_cast<int64_t>(bytes)); }
+
+SharedComm::SharedComm(const std::vector<int>& cudaDevices, size_t poolBytes) : mDevices(cudaDevices) {
+    const int n = static_cast<int>(cudaDevices.size());
+    bool distinct = n > 1;
+    for (int i = 1; i < n; ++i) distinct = distinct && cudaDevices[static_cast<size_t>(i)] != cudaDevices[0];
+    Check(dt_comm_create(n, cudaDevices.data(), 0, &mComm), "dt_comm_create");
     const char* t = std::getenv("DTORCH_COMM_TIMEOUT_SECOND");
     if (t != nullptr && std::atoll(t) > 0) Check(dt_comm_set_timeout_ms(mComm, std::atoll(t) * 1000), "dt_comm_set_timeout_ms");
+    if (poolBytes == 0 || !distinct || dt_comm_same_device(mComm)) return;
+    // the symmetric pool: the NVLS buffer where the switch supports it (all-reduces on it reduce in the
+    // switch), else a symmetric heap of the same size
+    int nvls = 0;
+    bool use_nvls = dt_comm_nvls_supported(mComm, &nvls) == DT_OK && nvls && dt_comm_nvls_alloc(mComm, poolBytes) == DT_OK;
+    if (!use_nvls) {
+        dt_comm_destroy(mComm);
+        mComm = nullptr;
+        Check(dt_comm_create(n, cudaDevices.data(), poolBytes, &mComm), "dt_comm_create");
+        if (t != nullptr && std::atoll(t) > 0) Check(dt_comm_set_timeout_ms(mComm, std::atoll(t) * 1000), "dt_comm_set_timeout_ms");
+    }
+    std::vector<char*> bases;
+    size_t bytes = 0;
+    for (int r = 0; r < n; ++r) {
+        void* base = nullptr;
+        size_t b = 0;
+        Check(use_nvls ? dt_comm_nvls_buffer(mComm, r, &base, &b) : dt_comm_heap(mComm, r, &base, &b), "pool base");
+        bases.push_back(static_cast<char*>(base));
+        bytes = (r == 0) ? b : std::min(bytes, b);
+    }
+    mPool = std::make_unique<SymmetricPool>(cudaDevices, bases, bytes, use_nvls);
 }
 
 SharedComm::~SharedComm() {
+    mPool.reset();
     if (mComm != nullptr) dt_comm_destroy(mComm);
 }
 
@@ -114,22 +155,17 @@ c10::intrusive_ptr<c10d::Work> P2PBackend::allgather(std::vector<std::vector<at:
         auto& outs = outputs[i];
         TORCH_CHECK(static_cast<int>(outs.size()) == getSize(), "allgather: one output per rank");
         at::Tensor in = inputs[i].contiguous();
-        std::vector<int64_t> lens;
-        int64_t total = 0;
+        std::vector<void*> out_ptrs;
+        std::vector<size_t> room;
         for (auto& o : outs) {
-            lens.push_back(o.numel());
-            total += o.numel();
+            TORCH_CHECK(o.is_contiguous(), "allgather: contiguous outputs");
+            out_ptrs.push_back(o.data_ptr());
+            room.push_back(static_cast<size_t>(o.nbytes()));
         }
-        TORCH_CHECK(lens[static_cast<size_t>(getRank())] == in.numel(), "allgather: own output size must match input");
-        at::Tensor flat = at::empty({total}, in.options());
-        Check(dt_all_gather(comm(), getRank(), in.data_ptr(), flat.data_ptr(), 1, lens.data(),
-                            static_cast<size_t>(in.element_size()), CurrentStream(cudaDevice())),
-              "dt_all_gather");
-        int64_t off = 0;
-        for (auto& o : outs) {
-            o.copy_(flat.narrow(0, off, o.numel()).view(o.sizes()));
-            off += o.numel();
-        }
+        // every rank's input lands in its own output tensor of every rank, in one launch
+        Check(dt_all_gather_list(comm(), getRank(), in.data_ptr(), static_cast<size_t>(in.nbytes()), out_ptrs.data(),
+                                 room.data(), CurrentStream(cudaDevice())),
+              "dt_all_gather_list");
     }
     return Done();
 }
@@ -149,21 +185,22 @@ c10::intrusive_ptr<c10d::Work> P2PBackend::alltoall(std::vector<at::Tensor>& out
                                                     const c10d::AllToAllOptions&) {
     const int n = getSize();
     TORCH_CHECK(static_cast<int>(inputs.size()) == n && static_cast<int>(outputs.size()) == n, "alltoall: one tensor per rank");
-    const int64_t chunk = inputs[0].numel();
-    for (int k = 0; k < n; ++k)
-        TORCH_CHECK(inputs[k].numel() == chunk && outputs[k].numel() == chunk,
-                    "dtorch_b200 alltoall (list form) needs equal chunks; ThreadGroup::AllToAll handles uneven shards");
-    // every rank's input viewed as [1, n, chunk]: split along dim 1, chunk k -> rank k, concat along dim 0
-    std::vector<at::Tensor> flat_in;
-    for (auto& t : inputs) flat_in.push_back(t.reshape({-1}));
-    at::Tensor in = at::cat(flat_in, 0).contiguous();
-    at::Tensor out = at::empty({n, chunk}, in.options());
-    const int64_t shape[3] = {1, n, chunk};
-    std::vector<int64_t> lens(static_cast<size_t>(n), 1);
-    Check(dt_all_to_all(comm(), getRank(), in.data_ptr(), out.data_ptr(), 3, shape, 0, 1, lens.data(),
-                        static_cast<size_t>(in.element_size()), CurrentStream(cudaDevice())),
-          "dt_all_to_all");
-    for (int k = 0; k < n; ++k) outputs[k].copy_(out[k].view(outputs[k].sizes()));
+    // inputs[k] goes to rank k, outputs[k] receives rank k's chunk: one launch of peer stores, no cat / copy
+    std::vector<at::Tensor> ins;
+    std::vector<const void*> in_ptrs;
+    std::vector<void*> out_ptrs;
+    std::vector<size_t> in_bytes, room;
+    for (int k = 0; k < n; ++k) {
+        ins.push_back(inputs[k].contiguous());
+        TORCH_CHECK(outputs[k].is_contiguous(), "alltoall: contiguous outputs");
+        in_ptrs.push_back(ins.back().data_ptr());
+        in_bytes.push_back(static_cast<size_t>(ins.back().nbytes()));
+        out_ptrs.push_back(outputs[k].data_ptr());
+        room.push_back(static_cast<size_t>(outputs[k].nbytes()));
+    }
+    Check(dt_all_to_all_list(comm(), getRank(), in_ptrs.data(), in_bytes.data(), out_ptrs.data(), room.data(),
+                             CurrentStream(cudaDevice())),
+          "dt_all_to_all_list");
     return Done();
 }
 
@@ -184,6 +221,14 @@ ThreadGroup::ThreadGroup(std::shared_ptr<SharedComm> comm, const std::vector<int
 
 void* ThreadGroup::Stream() const { return CurrentStream(mComm->CudaDevice(mRank)); }
 
+torch::Tensor ThreadGroup::NewOutput(at::IntArrayRef shape, const at::TensorOptions& opts, size_t bytesAllRanks) {
+    if (SymmetricPool* pool = mComm->Pool()) {
+        torch::Tensor t = pool->Empty(mRank, shape, opts, bytesAllRanks, static_cast<cudaStream_t>(Stream()), mComm);
+        if (t.defined()) return t;
+    }
+    return torch::empty(shape, opts);
+}
+
 void ThreadGroup::CheckInput(const torch::Tensor& t) const {
     TORCH_CHECK(t.is_cuda(), "ThreadGroup: the B200 collectives take CUDA tensors (no CPU fallback)");
     TORCH_CHECK(t.get_device() == mComm->CudaDevice(mRank), "ThreadGroup: tensor on cuda:", t.get_device(),
@@ -195,7 +240,7 @@ void ThreadGroup::Barrier() { mBackend->barrier(); }
 torch::Tensor ThreadGroup::AllReduce(const torch::Tensor& input, ReduceOpType) {
     CheckInput(input);
     torch::Tensor in = input.contiguous();
-    torch::Tensor out = torch::empty_like(in);
+    torch::Tensor out = NewOutput(in.sizes(), in.options(), static_cast<size_t>(in.nbytes()));
     Check(dt_all_reduce(mComm->get(), mRank, in.data_ptr(), out.data_ptr(), static_cast<size_t>(in.numel()),
                         DTypeCode(in.scalar_type()), DT_SUM, DT_ACCUM_FP32, Stream()),
           "dt_all_reduce");
@@ -213,7 +258,7 @@ torch::Tensor ThreadGroup::EqualShapeAllGatherIntoTensor(const torch::Tensor& in
     auto shape = in.sizes().vec();
     const int64_t rows = shape[0];
     shape[0] *= mSize;
-    torch::Tensor out = torch::empty(shape, in.options());
+    torch::Tensor out = NewOutput(shape, in.options(), static_cast<size_t>(in.nbytes()) * static_cast<size_t>(mSize));
     std::vector<int64_t> lens(static_cast<size_t>(mSize), rows);
     const size_t inner = static_cast<size_t>(rows == 0 ? 0 : in.numel() / rows) * in.element_size();
     Check(dt_all_gather(mComm->get(), mRank, in.data_ptr(), out.data_ptr(), 1, lens.data(), inner, Stream()),
@@ -233,7 +278,7 @@ torch::Tensor ThreadGroup::AllGather(const torch::Tensor& input, const LocalShap
     const int64_t outer = Prod(shape, 0, d);
     const int64_t inner = Prod(shape, d + 1, shape.size()) * in.element_size();
     shape[d] = std::accumulate(lens.begin(), lens.end(), int64_t{0});
-    torch::Tensor out = torch::empty(shape, in.options());
+    torch::Tensor out = NewOutput(shape, in.options(), static_cast<size_t>(Prod(shape, 0, shape.size()) * in.element_size()));
     Check(dt_all_gather(mComm->get(), mRank, in.data_ptr(), out.data_ptr(), static_cast<size_t>(outer), lens.data(),
                         static_cast<size_t>(inner), Stream()),
           "dt_all_gather");
@@ -251,7 +296,7 @@ std::vector<torch::Tensor> ThreadGroup::AllGatherIntoVec(const torch::Tensor& in
     }
     TORCH_CHECK(lens[static_cast<size_t>(mRank)] == in.numel(), "AllGatherIntoVec: local shape disagrees with the operand");
     const int64_t total = std::accumulate(lens.begin(), lens.end(), int64_t{0});
-    torch::Tensor flat = torch::empty({total}, in.options());
+    torch::Tensor flat = NewOutput({total}, in.options(), static_cast<size_t>(total * in.element_size()));
     Check(dt_all_gather(mComm->get(), mRank, in.data_ptr(), flat.data_ptr(), 1, lens.data(),
                         static_cast<size_t>(in.element_size()), Stream()),
           "dt_all_gather");
@@ -271,7 +316,7 @@ torch::Tensor ThreadGroup::ReduceScatterTensor(const torch::Tensor& input, Reduc
     torch::Tensor in = input.contiguous();
     auto shape = in.sizes().vec();
     shape[0] /= mSize;
-    torch::Tensor out = torch::empty(shape, in.options());
+    torch::Tensor out = NewOutput(shape, in.options(), static_cast<size_t>(in.nbytes()) / static_cast<size_t>(mSize));
     Check(dt_reduce_scatter(mComm->get(), mRank, in.data_ptr(), out.data_ptr(), static_cast<size_t>(out.numel()),
                             DTypeCode(in.scalar_type()), DT_SUM, DT_ACCUM_FP32, Stream()),
           "dt_reduce_scatter");
@@ -288,8 +333,12 @@ torch::Tensor ThreadGroup::AllToAll(const torch::Tensor& input, size_t srcDim, s
     TORCH_CHECK(srcLens[static_cast<size_t>(mRank)] == shape[srcDim], "AllToAll: local shape disagrees with the operand");
     auto out_shape = shape;
     out_shape[srcDim] = std::accumulate(srcLens.begin(), srcLens.end(), int64_t{0});
-    out_shape[destDim] = ShardSizes(shape[destDim], mSize)[static_cast<size_t>(mRank)];
-    torch::Tensor out = torch::empty(out_shape, in.options());
+    const auto destSplit = ShardSizes(shape[destDim], mSize);
+    out_shape[destDim] = destSplit[static_cast<size_t>(mRank)];
+    auto max_shape = out_shape;
+    max_shape[destDim] = destSplit[0];  // the first ranks get the larger chunk
+    torch::Tensor out = NewOutput(out_shape, in.options(),
+                                  static_cast<size_t>(Prod(max_shape, 0, max_shape.size()) * in.element_size()));
     Check(dt_all_to_all(mComm->get(), mRank, in.data_ptr(), out.data_ptr(), static_cast<int>(shape.size()), shape.data(),
                         static_cast<int>(srcDim), static_cast<int>(destDim), srcLens.data(),
                         static_cast<size_t>(in.element_size()), Stream()),
@@ -314,12 +363,16 @@ std::vector<torch::Tensor> ThreadGroup::AllToAllMulti(const std::vector<torch::T
     TORCH_CHECK(srcLens[static_cast<size_t>(mRank)] == shape[srcDim], "AllToAllMulti: local shape disagrees with the operand");
     auto out_shape = shape;
     out_shape[srcDim] = std::accumulate(srcLens.begin(), srcLens.end(), int64_t{0});
-    out_shape[destDim] = ShardSizes(shape[destDim], mSize)[static_cast<size_t>(mRank)];
+    const auto destSplit = ShardSizes(shape[destDim], mSize);
+    out_shape[destDim] = destSplit[static_cast<size_t>(mRank)];
+    auto max_shape = out_shape;
+    max_shape[destDim] = destSplit[0];
+    const size_t max_bytes = static_cast<size_t>(Prod(max_shape, 0, max_shape.size()) * ins[0].element_size());
     std::vector<torch::Tensor> outs;
     std::vector<const void*> in_ptrs;
     std::vector<void*> out_ptrs;
     for (auto& t : ins) {
-        outs.push_back(torch::empty(out_shape, t.options()));
+        outs.push_back(NewOutput(out_shape, t.options(), max_bytes));
         in_ptrs.push_back(t.data_ptr());
         out_ptrs.push_back(outs.back().data_ptr());
     }
@@ -363,7 +416,7 @@ ThreadGroup& ThreadGroupManager::GetThreadGroup(const std::vector<int64_t>& allD
         entry = std::make_unique<Entry>();
         std::vector<int> devices;
         for (auto id : allDeviceId) devices.push_back(CudaDeviceOf(id));
-        entry->comm = std::make_shared<SharedComm>(devices);
+        entry->comm = std::make_shared<SharedComm>(devices, PoolBytes());
         entry->ranks.resize(static_cast<size_t>(size));
     }
     auto& tg = entry->ranks[static_cast<size_t>(rank)];

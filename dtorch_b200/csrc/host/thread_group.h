@@ -15,6 +15,7 @@
 #include <torch/torch.h>
 
 #include "../../../include/dtorch_b200.h"
+#include "sym_pool.h"
 
 namespace dtb {
 
@@ -33,20 +34,28 @@ struct LocalShapes {
     bool IsEvenSplit() const;
 };
 
-// One dt_comm shared by the rank threads of a group.
+// Bytes of the symmetric pool each new peer-mode group gets (0 = none): DTORCH_B200_POOL_MB, or the value set
+// through SetPoolBytes, which wins for groups created after the call.
+size_t PoolBytes();
+void SetPoolBytes(size_t bytes);
+
+// One dt_comm shared by the rank threads of a group, and the group's symmetric pool: the communicator's NVLS
+// buffer when every device supports NVLink multicast, else its symmetric heap.
 class SharedComm {
 public:
-    explicit SharedComm(const std::vector<int>& cudaDevices);
+    SharedComm(const std::vector<int>& cudaDevices, size_t poolBytes);
     ~SharedComm();
     SharedComm(const SharedComm&) = delete;
     SharedComm& operator=(const SharedComm&) = delete;
     dt_comm* get() const { return mComm; }
     int CudaDevice(int rank) const { return mDevices[static_cast<size_t>(rank)]; }
     int Size() const { return static_cast<int>(mDevices.size()); }
+    SymmetricPool* Pool() const { return mPool.get(); }
 
 private:
     dt_comm* mComm = nullptr;
     std::vector<int> mDevices;
+    std::unique_ptr<SymmetricPool> mPool;
 };
 
 // Throws std::runtime_error carrying the status name and detail for a non-zero dt_status.
@@ -89,6 +98,12 @@ public:
     int64_t GetGlobalDeviceId() const { return mIds[static_cast<size_t>(mRank)]; }
     const std::vector<int64_t>& GetAllGlobalDeviceId() const { return mIds; }
     P2PBackend& Backend() { return *mBackend; }
+
+    // A new tensor on this rank's device for a collective's output: from the group's symmetric pool when it has
+    // one (every rank of the group must make the same sequence of these calls, with the same `bytesAllRanks`,
+    // the largest of the ranks' sizes), else torch::empty.
+    torch::Tensor NewOutput(at::IntArrayRef shape, const at::TensorOptions& opts, size_t bytesAllRanks);
+    SymmetricPool* Pool() const { return mComm->Pool(); }
 
     void Barrier();
 

@@ -203,6 +203,43 @@ def _merge_same_shard_dims(mesh: torch.Tensor, placements: List[Placement]):
     return mesh.permute(perm).reshape(new_shape), new_p
 
 
+def set_pool_bytes(nbytes: int) -> None:
+    """Give every device group created from now on a symmetric pool of `nbytes` per GPU (0: none; the default
+    comes from DTORCH_B200_POOL_MB). DTensor locals placed by ``from_torch`` / ``empty`` on a 1-D mesh and the
+    outputs of every collective then sit at the same offset on every GPU of the group, so collectives on them
+    need no pointer exchange; where the GPUs support NVLink multicast the pool is the group's NVLS buffer and
+    all-reduces on it reduce inside the NVSwitch (fp32 accumulation, the switch's order: within the reductions'
+    tolerance rather than bit-identical to the rank-order fold). Call before the group's first collective."""
+    _host.set_pool_bytes(int(nbytes))
+
+
+def _pool_group(device_mesh: DeviceMesh) -> Optional[List[int]]:
+    """The device group whose pool holds the locals of a DTensor on `device_mesh` (1-D peer meshes only)."""
+    if device_mesh.ndim != 1 or len(device_mesh.ids) < 2 or _host.pool_bytes() == 0:
+        return None
+    if os.environ.get("DTORCH_DTENSOR_IN_SAME_DEVICE") == "1":
+        return None
+    return device_mesh.ids
+
+
+def _place_locals(parts: Dict[int, torch.Tensor], device_mesh: DeviceMesh) -> Dict[int, torch.Tensor]:
+    """Each device's part on its GPU: in the group's symmetric pool when it has one (one block per device,
+    sized for the largest part, in mesh order on every device), else an ordinary allocation."""
+    group = _pool_group(device_mesh)
+    out: Dict[int, torch.Tensor] = {}
+    if group is not None:
+        nbytes = max(t.numel() * t.element_size() for t in parts.values())
+        for gid in group:
+            t = parts[gid]
+            dst = _host.pool_empty(group, gid, list(t.shape), t.dtype, nbytes)
+            dst.copy_(t)
+            out[gid] = dst
+        return out
+    for gid, t in parts.items():
+        out[gid] = t.contiguous().to(f"cuda:{cuda_device_of(gid)}")
+    return out
+
+
 class DTensor:
     """A distributed tensor: one local tensor per global device id of `device_mesh`."""
 
@@ -224,6 +261,23 @@ class DTensor:
     def locals(self) -> Dict[int, torch.Tensor]:
         return dict(self._locals)
 
+    @staticmethod
+    def empty(shapes: Dict[int, Sequence[int]], dtype, device_mesh: DeviceMesh, placements: Sequence[Placement],
+              shape: Sequence[int]) -> "DTensor":
+        """A DTensor of uninitialised locals with the given per-device shapes, allocated like ``from_torch``'s
+        (in the group's symmetric pool when it has one)."""
+        group = _pool_group(device_mesh)
+        es = torch.tensor([], dtype=dtype).element_size()
+        out: Dict[int, torch.Tensor] = {}
+        if group is not None:
+            nbytes = max(math.prod(s) * es for s in shapes.values())
+            for gid in group:
+                out[gid] = _host.pool_empty(group, gid, list(shapes[gid]), dtype, nbytes)
+        else:
+            for gid in device_mesh.ids:
+                out[gid] = torch.empty(list(shapes[gid]), dtype=dtype, device=f"cuda:{cuda_device_of(gid)}")
+        return DTensor(out, device_mesh, placements, shape)
+
     # -- placement of a whole tensor (host helpers) -------------------------------------------------------
     @staticmethod
     def from_torch(tensor: torch.Tensor, device_mesh: DeviceMesh, placements: Sequence[Placement]) -> "DTensor":
@@ -231,12 +285,11 @@ class DTensor:
         placements = [Placement(p) for p in placements]
         _host.check_valid(list(tensor.shape), list(device_mesh.shape), device_mesh.ids, _strings(placements))
         mesh, plc = _merge_same_shard_dims(device_mesh.mesh, placements)
-        out: Dict[int, torch.Tensor] = {}
+        parts_of: Dict[int, torch.Tensor] = {}
 
         def scatter(t: torch.Tensor, m: torch.Tensor, i: int):
             if i == len(plc):
-                gid = int(m.reshape(-1)[0])
-                out[gid] = t.contiguous().to(f"cuda:{cuda_device_of(gid)}")
+                parts_of[int(m.reshape(-1)[0])] = t
                 return
             n = m.shape[0]
             p = plc[i]
@@ -257,7 +310,7 @@ class DTensor:
                 scatter(parts[k], m[k], i + 1)
 
         scatter(tensor, mesh, 0)
-        return DTensor(out, device_mesh, placements, tensor.shape)
+        return DTensor(_place_locals(parts_of, device_mesh), device_mesh, placements, tensor.shape)
 
     def to_torch(self, device: Union[str, torch.device] = "cpu") -> torch.Tensor:
         mesh, plc = _merge_same_shard_dims(self.device_mesh.mesh, self.placements)

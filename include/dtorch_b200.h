@@ -165,6 +165,22 @@ int dt_all_to_all_multi(dt_comm* comm, int rank, int ntensors, const void* const
                         const int64_t* in_shape, int src_dim, int dst_dim, const int64_t* src_lens, size_t elem_bytes,
                         void* stream);
 
+/* The list form of c10d's alltoall (the virtual ThreadGroup::AllToAll calls, thread_group.cc:236, and the
+ * same-device backend's alltoall, thread_group_same_device_backend.cc:276-302): ins[k] (in_bytes[k] bytes) is
+ * this rank's buffer for rank k, outs[k] (room for out_bytes[k] bytes) receives rank k's buffer for this rank.
+ * One launch moves every pair with peer stores; no concatenation or staging copy. Single-process
+ * communicators (peer or same-device mode): the ranks exchange their buffer lists in process. Every rank checks
+ * every pair (a send larger than its destination's room is DT_ERR_INVALID on all ranks). */
+int dt_all_to_all_list(dt_comm* comm, int rank, const void* const* ins, const size_t* in_bytes, void* const* outs,
+                       const size_t* out_bytes, void* stream);
+
+/* The list form of c10d's allgather (ThreadGroup::AllGatherIntoVec, thread_group.cc:173-190; same-device
+ * allgather, thread_group_same_device_backend.cc:177-201): `in` (in_bytes) goes to every rank; outs[k] (room for
+ * out_bytes[k] bytes) receives rank k's input. Shards of different sizes are fine. Single-process
+ * communicators, checked like dt_all_to_all_list. */
+int dt_all_gather_list(dt_comm* comm, int rank, const void* in, size_t in_bytes, void* const* outs,
+                       const size_t* out_bytes, void* stream);
+
 /* Device-side barrier of all ranks on their streams. Replaces ThreadGroup::Barrier (thread_group.cc:118-125). */
 int dt_barrier(dt_comm* comm, int rank, void* stream);
 

@@ -581,3 +581,70 @@ def test_peer_reduce_scatter_fp16_odd_chunks(out_count):
             assert np.array_equal(np_raw(outs[r]), want[r]), r
     finally:
         comm.destroy()
+
+
+@pytest.mark.parametrize("mode", ["same", "peer"])
+@pytest.mark.parametrize("n", [2, 3, 8])
+def test_list_forms_match_restatement(mode, n):
+    """dt_all_to_all_list / dt_all_gather_list (c10d's list-form alltoall / allgather, one buffer per peer, uneven
+    sizes, misaligned lengths): rank k's outs[i] holds exactly rank i's ins[k] (all-to-all) or rank i's input
+    (all-gather), in one launch."""
+    devs = devices_for(n, mode)
+    rng = np.random.default_rng(77 + n)
+    comm = capi.Comm(devs)
+    try:
+        comm.set_timeout_ms(20000)
+        for it in range(4):
+            sizes = rng.integers(0, 40000, size=(n, n))  # bytes rank i sends to rank k
+            sizes[0, n - 1] = 1 + (it % 15)  # odd lengths force the narrow vector widths
+            src = [[torch.randint(0, 255, (int(sizes[i, k]),), dtype=torch.uint8, device=f"cuda:{devs[i]}")
+                    for k in range(n)] for i in range(n)]
+            dst = [[torch.full((int(sizes[i, k]) + 5,), 7, dtype=torch.uint8, device=f"cuda:{devs[k]}")
+                    for i in range(n)] for k in range(n)]
+            gin = [torch.randint(0, 255, (int(sizes[i, 0]),), dtype=torch.uint8, device=f"cuda:{devs[i]}")
+                   for i in range(n)]
+            gout = [[torch.full((int(sizes[i, 0]),), 9, dtype=torch.uint8, device=f"cuda:{devs[k]}")
+                     for i in range(n)] for k in range(n)]
+
+            def fn(r):
+                with torch.cuda.device(devs[r]):
+                    s = torch.cuda.current_stream(devs[r]).cuda_stream
+                    comm.all_to_all_list(r, [t.data_ptr() for t in src[r]], [t.numel() for t in src[r]],
+                                         [t.data_ptr() for t in dst[r]], [t.numel() for t in dst[r]], s)
+                    comm.all_gather_list(r, gin[r].data_ptr(), gin[r].numel(), [t.data_ptr() for t in gout[r]],
+                                         [t.numel() for t in gout[r]], s)
+                    torch.cuda.current_stream(devs[r]).synchronize()
+
+            run_ranks(n, fn)
+            for k in range(n):
+                for i in range(n):
+                    m = int(sizes[i, k])
+                    got = dst[k][i].cpu()
+                    assert torch.equal(got[:m], src[i][k].cpu()), (it, i, k)
+                    assert torch.all(got[m:] == 7), "wrote past the sent bytes"
+                    assert torch.equal(gout[k][i].cpu(), gin[i].cpu()), (it, i, k)
+        assert comm.error(0) == capi.DT_OK
+    finally:
+        comm.destroy()
+
+
+def test_list_form_rejects_oversized_sends_on_every_rank():
+    n = 2
+    comm = capi.Comm([0] * n)
+    try:
+        bufs = [torch.zeros(64, dtype=torch.uint8, device="cuda:0") for _ in range(4)]
+        errs = [None] * n
+
+        def fn(r):
+            try:
+                # rank 0 sends 64 bytes to rank 1, which offers room for 32
+                room = [64, 64] if r == 0 else [32, 64]
+                comm.all_to_all_list(r, [bufs[0].data_ptr(), bufs[1].data_ptr()], [64, 64],
+                                     [bufs[2].data_ptr(), bufs[3].data_ptr()], room)
+            except capi.DtError as e:
+                errs[r] = e.status
+
+        run_ranks(n, fn)
+        assert errs == [capi.DT_ERR_INVALID] * n
+    finally:
+        comm.destroy()
