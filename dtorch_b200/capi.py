@@ -75,6 +75,8 @@ SIGNATURES = [
     ("dt_local_all_reduce_host_noalloc", _I, [_I, _P, _P, _SZ, _I, _I, _P]),
     ("dt_all_to_all_list", _I, [_P, _I, _P, _P, _P, _P, _P]),
     ("dt_all_gather_list", _I, [_P, _I, _P, _SZ, _P, _P, _P]),
+    ("dt_all_gather_sub_split", _I, [_P, _I, _P, _P, _SZ, _P, _P, _SZ, _P]),
+    ("dt_peer_copy", _I, [_P, _I, _P, _I, _SZ, _P]),
 ]
 
 
@@ -248,6 +250,10 @@ class Comm:
         check(lib().dt_all_gather(self._h, rank, inp, out, outer, i64_array(lens), inner_bytes, stream),
               "dt_all_gather")
 
+    def all_gather_sub_split(self, rank, inp, out, outer, lens, fronts, inner_bytes, stream=0):
+        check(lib().dt_all_gather_sub_split(self._h, rank, inp, out, outer, i64_array(lens), i64_array(fronts),
+                                            inner_bytes, stream), "dt_all_gather_sub_split")
+
     def all_to_all(self, rank, inp, out, in_shape, src_dim, dst_dim, src_lens, elem_bytes, stream=0):
         check(lib().dt_all_to_all(self._h, rank, inp, out, len(in_shape), i64_array(in_shape), src_dim, dst_dim,
                                   i64_array(src_lens), elem_bytes, stream), "dt_all_to_all")
@@ -279,6 +285,11 @@ def local_all_reduce_host(host_ins, dev_ins, dev_out, host_out, count, dtype, fl
     copies in both directions overlapping the reduction; host_out is complete when `stream` reaches the call's end."""
     check(lib().dt_local_all_reduce_host(len(host_ins), ptr_array(host_ins), ptr_array(dev_ins), dev_out, host_out,
                                          count, dtype, flags, chunk_bytes, stream), "dt_local_all_reduce_host")
+
+
+def peer_copy(dst, dst_device, src, src_device, nbytes, stream=0):
+    """Kernel copy from src_device's memory into dst_device's over NVLink, on src_device's `stream`."""
+    check(lib().dt_peer_copy(dst, dst_device, src, src_device, nbytes, stream), "dt_peer_copy")
 
 
 NOALLOC_SCRATCH_BYTES = 32 << 20  # DT_NOALLOC_SCRATCH_BYTES

@@ -321,6 +321,7 @@ int pick_grid(K kernel, int dev, int num_sms, int64_t want_blocks, int per_sm_ca
 }
 
 constexpr int kReduceBlocksPerSM = 2;
+constexpr int kMultiSegs = 3 * kMaxRanks * kMaxRanks;  // same-device fused all-to-all: q, k, v at 8 ranks
 constexpr int kCopyBlocksPerSM = 2;
 
 // Upper bound on the CTAs of a peer (cross-GPU) launch; DTORCH_B200_P2P_CTAS overrides the default (no cap
@@ -1303,24 +1304,94 @@ int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t ou
 
 // ---- all-gather -------------------------------------------------------------------------------------------
 
-int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
-                  size_t inner_bytes, void* stream_v) {
+}  // extern "C"
+
+namespace {
+
+// Placement of rank r's shard in the gathered tensor, as 1 or 2 segments from `src` to `dst` (the output base):
+// without sub-split, rows [0, lens[r]) land at the concat offset of rank r; with sub-split (fronts != nullptr)
+// the first fronts[r] rows land among the front parts (all ranks' fronts first, in rank order) and the rest
+// among the back parts after them -- DistributeGather::GatherShardWithSubSplit,
+// dtorch/core/kernel/kernel_implement/distributed_scather_and_gather.cc:147-183.
+int gather_segs(int n, int r, const int64_t* lens, const int64_t* fronts, size_t outer, size_t inner_bytes,
+                const char* src, char* dst, Seg* out) {
+    int64_t total = 0, off = 0, ftotal = 0, foff = 0, boff = 0;
+    for (int i = 0; i < n; ++i) {
+        total += lens[i];
+        if (i < r) off += lens[i];
+        if (fronts != nullptr) {
+            ftotal += fronts[i];
+            if (i < r) {
+                foff += fronts[i];
+                boff += lens[i] - fronts[i];
+            }
+        }
+    }
+    const int64_t inner = static_cast<int64_t>(inner_bytes);
+    auto seg = [&](int64_t row0, int64_t rows, int64_t at) {
+        Seg g{};
+        g.src = src + row0 * inner;
+        g.dst = dst + at * inner;
+        g.run = rows * inner;
+        g.cnt[0] = g.cnt[1] = 1;
+        g.cnt[2] = static_cast<int64_t>(outer);
+        g.ss[2] = lens[r] * inner;
+        g.ds[2] = total * inner;
+        if (g.run == 0 || outer == 0) {
+            g.run = 0;
+            g.cnt[2] = 1;
+        }
+        return g;
+    };
+    if (fronts == nullptr) {
+        out[0] = seg(0, lens[r], off);
+        return 1;
+    }
+    out[0] = seg(0, fronts[r], foff);
+    out[1] = seg(fronts[r], lens[r] - fronts[r], ftotal + boff);
+    return 2;
+}
+
+int check_gather(int n, const int64_t* lens, const int64_t* fronts) {
+    if (lens == nullptr) return fail(DT_ERR_INVALID, "null lens");
+    for (int r = 0; r < n; ++r) {
+        if (lens[r] < 0) return fail(DT_ERR_INVALID, "negative shard length");
+        if (fronts != nullptr && (fronts[r] < 0 || fronts[r] > lens[r]))
+            return fail(DT_ERR_INVALID, "sub-split front part outside its shard");
+    }
+    return DT_OK;
+}
+
+// Every rank's shard (all on this device) into one output.
+int local_gather(int n, const void* const* ins, void* out, size_t outer, const int64_t* lens, const int64_t* fronts,
+                 size_t inner_bytes, cudaStream_t stream, int dev, int sms) {
+    CopyArgs<2 * kMaxRanks> a{};
+    a.nseg = 0;
+    for (int r = 0; r < n; ++r) {
+        if (ins[r] == nullptr && lens[r] > 0 && outer > 0 && inner_bytes > 0) return fail(DT_ERR_INVALID, "null input");
+        a.nseg += gather_segs(n, r, lens, fronts, outer, inner_bytes, static_cast<const char*>(ins[r]),
+                              static_cast<char*>(out), &a.seg[a.nseg]);
+    }
+    return launch_copy<2 * kMaxRanks, false>(a, dev, sms, stream);
+}
+
+int all_gather_impl(dt_comm* c, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
+                    const int64_t* fronts, size_t inner_bytes, void* stream_v) {
     DeviceGuard device_guard;
     int st = common_checks(c, rank);
     if (st != DT_OK) return st;
-    if (lens == nullptr) return fail(DT_ERR_INVALID, "null lens");
-    int64_t total = 0, off[kMaxRanks];
-    for (int r = 0; r < c->n; ++r) {
-        if (lens[r] < 0) return fail(DT_ERR_INVALID, "negative shard length");
-        off[r] = total;
-        total += lens[r];
-    }
+    st = check_gather(c->n, lens, fronts);
+    if (st != DT_OK) return st;
+    int64_t total = 0;
+    for (int r = 0; r < c->n; ++r) total += lens[r];
     const size_t in_bytes = outer * static_cast<size_t>(lens[rank]) * inner_bytes;
     const size_t out_bytes = outer * static_cast<size_t>(total) * inner_bytes;
     if ((in_bytes > 0 && in == nullptr) || (out_bytes > 0 && out == nullptr)) return fail(DT_ERR_INVALID, "null buffer");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
     RankState& s = c->r[rank];
     if (c->same_device) {
+        std::vector<int64_t> lv(lens, lens + c->n), fv;
+        if (fronts != nullptr) fv.assign(fronts, fronts + c->n);
         return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
             const void* ins[kMaxRanks];
             void* outs[kMaxRanks];
@@ -1331,8 +1402,10 @@ int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer,
                 for (int j = 0; j < nout; ++j) dup = dup || outs[j] == all[r].out;
                 if (!dup) outs[nout++] = all[r].out;
             }
+            if (out_bytes == 0) return DT_OK;
             for (int j = 0; j < nout; ++j) {
-                int rc = dt_local_all_gather(c->n, ins, outs[j], outer, lens, inner_bytes, st0);
+                const int rc = local_gather(c->n, ins, outs[j], outer, lv.data(), fv.empty() ? nullptr : fv.data(),
+                                            inner_bytes, st0, s.dev, s.num_sms);
                 if (rc != DT_OK) return rc;
             }
             return DT_OK;
@@ -1347,28 +1420,34 @@ int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer,
     char* outs[kMaxRanks];
     st = resolve_peers(c, rank, in, in_bytes, out, out_bytes, ins, outs);
     if (st != DT_OK) return st;
-    CopyArgs<kMaxRanks> a{};
+    CopyArgs<2 * kMaxRanks> a{};
     a.sig = make_sig(c, rank);
-    a.nseg = c->n;
+    a.nseg = 0;
     for (int j = 0; j < c->n; ++j) {
         const int k = (rank + 1 + j) % c->n;  // destinations in rotated order, own output last
-        Seg& sg = a.seg[j];
-        sg.src = static_cast<const char*>(in);
-        sg.dst = outs[k] + static_cast<size_t>(off[rank]) * inner_bytes;
-        sg.run = lens[rank] * static_cast<int64_t>(inner_bytes);
-        sg.cnt[0] = sg.cnt[1] = 1;
-        sg.cnt[2] = static_cast<int64_t>(outer);
-        sg.ss[2] = sg.run;
-        sg.ds[2] = total * static_cast<int64_t>(inner_bytes);
-        if (sg.run == 0 || outer == 0) {
-            sg.run = 0;
-            sg.cnt[2] = 1;
-        }
+        a.nseg += gather_segs(c->n, rank, lens, fronts, outer, inner_bytes, static_cast<const char*>(in), outs[k],
+                              &a.seg[a.nseg]);
     }
     int64_t max_len = 0;
     for (int r = 0; r < c->n; ++r) max_len = std::max(max_len, lens[r]);
+    // the grid depends only on sizes every rank shares
     const int64_t want = copy_want_blocks(max_len * static_cast<int64_t>(inner_bytes), static_cast<int64_t>(outer), c->n);
-    return launch_copy<kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+    return launch_copy<2 * kMaxRanks, true>(a, s.dev, s.num_sms, stream, want);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dt_all_gather(dt_comm* c, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
+                  size_t inner_bytes, void* stream_v) {
+    return all_gather_impl(c, rank, in, out, outer, lens, nullptr, inner_bytes, stream_v);
+}
+
+int dt_all_gather_sub_split(dt_comm* c, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
+                            const int64_t* fronts, size_t inner_bytes, void* stream_v) {
+    if (fronts == nullptr) return fail(DT_ERR_INVALID, "dt_all_gather_sub_split: null fronts");
+    return all_gather_impl(c, rank, in, out, outer, lens, fronts, inner_bytes, stream_v);
 }
 
 // ---- all-to-all -------------------------------------------------------------------------------------------
@@ -1470,12 +1549,42 @@ int dt_all_to_all_multi(dt_comm* c, int rank, int ntensors, const void* const* i
             return fail(DT_ERR_INVALID, "null buffer");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
     RankState& s = c->r[rank];
-    if (c->same_device || c->n == 1) {
+    if (c->n == 1) {
         for (int t = 0; t < ntensors; ++t) {
             st = dt_all_to_all(c, rank, ins_v[t], outs_v[t], ndim, in_shape, src_dim, dst_dim, src_lens, elem_b, stream_v);
             if (st != DT_OK) return st;
         }
         return DT_OK;
+    }
+    if (c->same_device) {
+        // one launch for every tensor of every rank: ntensors * n * n segments (at most 3 tensors at 8 ranks fit
+        // one launch's parameters; more run as one launch per tensor)
+        Slot mine{};
+        for (int t = 0; t < ntensors; ++t) {
+            mine.lin[t] = ins_v[t];
+            mine.extra[t] = outs_v[t];
+        }
+        return same_device_call(c, rank, mine, stream, [&](const Slot* all, cudaStream_t st0) -> int {
+            const int per = c->n * c->n;
+            for (int t0 = 0; t0 < ntensors;) {
+                const int nt = std::min(ntensors - t0, std::max(1, kMultiSegs / per));
+                CopyArgs<kMultiSegs> a{};
+                a.nseg = 0;
+                // interleaved: destination shift j, then tensor, then source rank
+                for (int j = 0; j < c->n; ++j)
+                    for (int t = t0; t < t0 + nt; ++t)
+                        for (int i = 0; i < c->n; ++i) {
+                            const int k = (i + j) % c->n;
+                            a.seg[a.nseg++] = a2a_seg(g, static_cast<const char*>(all[i].lin[t]),
+                                                      static_cast<char*>(all[k].extra[t]), src_lens[i], soff[i],
+                                                      split[k], doff[k]);
+                        }
+                const int rc = launch_copy<kMultiSegs, false>(a, s.dev, s.num_sms, st0);
+                if (rc != DT_OK) return rc;
+                t0 += nt;
+            }
+            return DT_OK;
+        });
     }
     DT_CUDA(cudaSetDevice(s.dev));
     // every rank's output pointers of every tensor, as addressed from this device
@@ -1803,6 +1912,62 @@ int dt_comm_nvls_buffer(dt_comm* c, int rank, void** ptr, size_t* bytes) {
     return DT_OK;
 }
 
+// ---- point-to-point move between two GPUs ---------------------------------------------------------------
+
+}  // extern "C"
+
+namespace {
+
+// Peer access from `from` to `to`, enabled once per ordered pair for the whole process.
+int ensure_peer_access(int from, int to) {
+    static std::mutex mu;
+    static std::vector<std::pair<int, int>> done;
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& p : done)
+        if (p.first == from && p.second == to) return DT_OK;
+    int can = 0;
+    DT_CUDA(cudaDeviceCanAccessPeer(&can, from, to));
+    if (!can) return fail(DT_ERR_PEER, "cudaDeviceCanAccessPeer = 0 for the two devices");
+    DT_CUDA(cudaSetDevice(from));
+    const cudaError_t e = cudaDeviceEnablePeerAccess(to, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+    } else if (e != cudaSuccess) {
+        return fail(DT_ERR_PEER, std::string("cudaDeviceEnablePeerAccess: ") + cudaGetErrorString(e));
+    }
+    done.emplace_back(from, to);
+    return DT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dt_peer_copy(void* dst, int dst_device, const void* src, int src_device, size_t bytes, void* stream) {
+    DeviceGuard device_guard;
+    if (bytes == 0) return DT_OK;
+    if (dst == nullptr || src == nullptr) return fail(DT_ERR_INVALID, "dt_peer_copy: null buffer");
+    int ndev = 0;
+    DT_CUDA(cudaGetDeviceCount(&ndev));
+    if (src_device < 0 || src_device >= ndev || dst_device < 0 || dst_device >= ndev)
+        return fail(DT_ERR_INVALID, "dt_peer_copy: device id out of range");
+    if (src_device != dst_device) {
+        const int st = ensure_peer_access(src_device, dst_device);
+        if (st != DT_OK) return st;
+    }
+    DT_CUDA(cudaSetDevice(src_device));
+    int sms = 0;
+    DT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, src_device));
+    CopyArgs<1> a{};
+    a.nseg = 1;
+    Seg& g = a.seg[0];
+    g.src = static_cast<const char*>(src);
+    g.dst = static_cast<char*>(dst);
+    g.run = static_cast<int64_t>(bytes);
+    g.cnt[0] = g.cnt[1] = g.cnt[2] = 1;
+    return launch_copy<1, false>(a, src_device, sms, static_cast<cudaStream_t>(stream));
+}
+
 // ---- same-device kernels ----------------------------------------------------------------------------------
 
 int dt_local_all_reduce(int n, const void* const* ins, void* out, size_t count, int dtype, int flags, void* stream) {
@@ -1914,36 +2079,17 @@ int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, si
 
 int dt_local_all_gather(int n, const void* const* ins, void* out, size_t outer, const int64_t* lens, size_t inner_bytes,
                         void* stream) {
-    if (n < 1 || n > kMaxRanks || ins == nullptr || lens == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
-    int64_t total = 0, off[kMaxRanks];
-    for (int r = 0; r < n; ++r) {
-        if (lens[r] < 0) return fail(DT_ERR_INVALID, "negative shard length");
-        off[r] = total;
-        total += lens[r];
-    }
+    if (n < 1 || n > kMaxRanks || ins == nullptr) return fail(DT_ERR_INVALID, "n must be 1..8");
+    int st = check_gather(n, lens, nullptr);
+    if (st != DT_OK) return st;
+    int64_t total = 0;
+    for (int r = 0; r < n; ++r) total += lens[r];
     if (outer * static_cast<size_t>(total) * inner_bytes == 0) return DT_OK;
     if (out == nullptr) return fail(DT_ERR_INVALID, "null out");
     int dev = 0, sms = 0;
-    int st = current_device_sms(&dev, &sms);
+    st = current_device_sms(&dev, &sms);
     if (st != DT_OK) return st;
-    CopyArgs<kMaxRanks> a{};
-    a.nseg = n;
-    for (int r = 0; r < n; ++r) {
-        Seg& sg = a.seg[r];
-        sg.src = static_cast<const char*>(ins[r]);
-        sg.dst = static_cast<char*>(out) + static_cast<size_t>(off[r]) * inner_bytes;
-        sg.run = lens[r] * static_cast<int64_t>(inner_bytes);
-        sg.cnt[0] = sg.cnt[1] = 1;
-        sg.cnt[2] = static_cast<int64_t>(outer);
-        sg.ss[2] = sg.run;
-        sg.ds[2] = total * static_cast<int64_t>(inner_bytes);
-        if (sg.run == 0) {
-            sg.cnt[2] = 1;
-        } else if (sg.src == nullptr) {
-            return fail(DT_ERR_INVALID, "null input");
-        }
-    }
-    return launch_copy<kMaxRanks, false>(a, dev, sms, static_cast<cudaStream_t>(stream));
+    return local_gather(n, ins, out, outer, lens, nullptr, inner_bytes, static_cast<cudaStream_t>(stream), dev, sms);
 }
 
 int dt_local_all_to_all(int n, const void* const* ins, void* const* outs, int ndim, const int64_t* in_shape,

@@ -84,21 +84,6 @@ bool PreCollectiveBarrier() {
     return s != nullptr && std::string(s) == "1";
 }
 
-// Reassemble a sub-split shard dim from every rank's piece (DistributeGather::GatherShardWithSubSplit,
-// distributed_scather_and_gather.cc:147-183, for a group that is the only mesh dim sharding `dim`): each
-// piece holds a front part of the first (subSplit + 1) rows and a back part of the rest.
-torch::Tensor GatherSubSplit(const std::vector<torch::Tensor>& pieces, int64_t dim, int64_t subSplit) {
-    const auto front_sizes = ShardSizes(subSplit + 1, static_cast<int64_t>(pieces.size()));
-    std::vector<torch::Tensor> fronts, backs;
-    for (size_t i = 0; i < pieces.size(); ++i) {
-        const int64_t len = pieces[i].size(dim);
-        TORCH_CHECK(front_sizes[i] < len, "sub-split piece smaller than its front part");
-        fronts.push_back(pieces[i].narrow(dim, 0, front_sizes[i]));
-        backs.push_back(pieces[i].narrow(dim, front_sizes[i], len - front_sizes[i]));
-    }
-    return torch::cat({torch::cat(fronts, dim), torch::cat(backs, dim)}, dim);
-}
-
 }  // namespace
 
 torch::Tensor ConvertPlacements(const torch::Tensor& input, const DeviceMesh& mesh, size_t meshDim, const Placement& src,
@@ -113,7 +98,8 @@ torch::Tensor ConvertPlacements(const torch::Tensor& input, const DeviceMesh& me
     }
     if (src.IsShard() && dst.IsReplicate()) {
         if (!src.HasSubSplit()) return src.dim == 0 ? tg.AllGatherIntoTensor(input, operand) : tg.AllGather(input, operand, src.dim);
-        return GatherSubSplit(tg.AllGatherIntoVec(input, operand), src.dim, src.subSplit);
+        // one launch places every rank's front and back pieces (the reference gathers, then concatenates twice)
+        return tg.AllGatherSubSplit(input, operand, src.dim, src.subSplit);
     }
     if (src.IsReplicate() && dst.IsShard()) return tg.ReplicateToShard(input, dst.dim, dst.subSplit);
     if (src.IsPartial() && dst.IsShard(0)) return tg.ReduceScatterTensor(input);

@@ -285,6 +285,31 @@ torch::Tensor ThreadGroup::AllGather(const torch::Tensor& input, const LocalShap
     return out;
 }
 
+torch::Tensor ThreadGroup::AllGatherSubSplit(const torch::Tensor& input, const LocalShapes& operand, int64_t shardIndex,
+                                             int64_t subSplit) {
+    CheckInput(input);
+    torch::Tensor in = input.contiguous();
+    auto shape = in.sizes().vec();
+    const size_t d = static_cast<size_t>(shardIndex);
+    TORCH_CHECK(d < shape.size(), "AllGatherSubSplit: shard dim out of range");
+    std::vector<int64_t> lens;
+    for (auto id : mIds) lens.push_back(operand.Get(id)[d]);
+    TORCH_CHECK(lens[static_cast<size_t>(mRank)] == shape[d], "AllGatherSubSplit: local shape disagrees with the operand");
+    // rank i's front piece: its share of the first subSplit + 1 rows (the reference's splitSize,
+    // distributed_scather_and_gather.cc:166-170)
+    const auto fronts = ShardSizes(subSplit + 1, mSize);
+    for (size_t i = 0; i < lens.size(); ++i)
+        TORCH_CHECK(fronts[i] < lens[i], "sub-split piece smaller than its front part");
+    const int64_t outer = Prod(shape, 0, d);
+    const int64_t inner = Prod(shape, d + 1, shape.size()) * in.element_size();
+    shape[d] = std::accumulate(lens.begin(), lens.end(), int64_t{0});
+    torch::Tensor out = NewOutput(shape, in.options(), static_cast<size_t>(Prod(shape, 0, shape.size()) * in.element_size()));
+    Check(dt_all_gather_sub_split(mComm->get(), mRank, in.data_ptr(), out.data_ptr(), static_cast<size_t>(outer),
+                                  lens.data(), fronts.data(), static_cast<size_t>(inner), Stream()),
+          "dt_all_gather_sub_split");
+    return out;
+}
+
 std::vector<torch::Tensor> ThreadGroup::AllGatherIntoVec(const torch::Tensor& input, const LocalShapes& operand) {
     CheckInput(input);
     torch::Tensor in = input.contiguous();

@@ -114,6 +114,10 @@ public:
     torch::Tensor EqualShapeAllGatherIntoTensor(const torch::Tensor& input);
     // S(shardIndex) -> R, uneven shards allowed; the concat along shardIndex happens inside the kernel
     torch::Tensor AllGather(const torch::Tensor& input, const LocalShapes& operand, int64_t shardIndex);
+    // Shard(shardIndex, subSplit) -> R: every rank's front piece (of the first subSplit + 1 rows) in rank order,
+    // then every rank's back piece, placed by the gather kernel itself
+    torch::Tensor AllGatherSubSplit(const torch::Tensor& input, const LocalShapes& operand, int64_t shardIndex,
+                                    int64_t subSplit);
     // every rank's tensor (views of one gathered buffer)
     std::vector<torch::Tensor> AllGatherIntoVec(const torch::Tensor& input, const LocalShapes& operand);
     // P -> S0, dim 0 divisible by the group size

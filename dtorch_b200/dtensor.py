@@ -203,6 +203,27 @@ def _merge_same_shard_dims(mesh: torch.Tensor, placements: List[Placement]):
     return mesh.permute(perm).reshape(new_shape), new_p
 
 
+def _to_device(t: torch.Tensor, device: int) -> torch.Tensor:
+    """`t` on CUDA device `device`: itself when it is there already, else a new tensor filled by dt_peer_copy (a
+    kernel on t's GPU storing into the destination over NVLink), ordered after the current streams of both
+    devices and before later work on the destination's current stream."""
+    if t.device.type != "cuda":
+        return t.to(f"cuda:{device}")
+    if t.device.index == device:
+        return t
+    from . import capi
+
+    t = t.contiguous()
+    src = t.device.index
+    out = torch.empty(t.shape, dtype=t.dtype, device=f"cuda:{device}")
+    s_src, s_dst = torch.cuda.current_stream(src), torch.cuda.current_stream(device)
+    s_src.wait_stream(s_dst)  # the destination buffer is free once the destination's stream got here
+    capi.peer_copy(out.data_ptr(), device, t.data_ptr(), src, t.numel() * t.element_size(), s_src.cuda_stream)
+    s_dst.wait_stream(s_src)
+    out.record_stream(s_src)
+    return out
+
+
 def set_pool_bytes(nbytes: int) -> None:
     """Give every device group created from now on a symmetric pool of `nbytes` per GPU (0: none; the default
     comes from DTORCH_B200_POOL_MB). DTensor locals placed by ``from_torch`` / ``empty`` on a 1-D mesh and the
@@ -315,9 +336,13 @@ class DTensor:
     def to_torch(self, device: Union[str, torch.device] = "cpu") -> torch.Tensor:
         mesh, plc = _merge_same_shard_dims(self.device_mesh.mesh, self.placements)
 
+        dev = torch.device(device)
+
         def gather(m: torch.Tensor, i: int) -> torch.Tensor:
             if i == len(plc):
-                return self._locals[int(m.reshape(-1)[0])].to(device)
+                t = self._locals[int(m.reshape(-1)[0])]
+                return _to_device(t, dev.index if dev.index is not None else torch.cuda.current_device()) \
+                    if dev.type == "cuda" else t.to(dev)
             p = plc[i]
             if p.is_replicate():
                 return gather(m[0], i + 1)
@@ -360,9 +385,9 @@ class DTensor:
             raise ValueError(f"device meshes differ in shape: {self.device_mesh.shape} vs {mesh.shape}")
         out = {}
         for src, dst in zip(self.device_mesh.ids, mesh.ids):
-            t = self._locals[src]
-            # a peer copy over NVLink between the two GPUs, ordered on both devices' current streams
-            out[dst] = t.to(f"cuda:{cuda_device_of(dst)}", non_blocking=True)
+            # rank i of the source mesh hands its local to rank i of the destination mesh: a kernel on the
+            # source GPU stores it straight into the destination GPU's memory over NVLink
+            out[dst] = _to_device(self._locals[src], cuda_device_of(dst))
         return DTensor(out, mesh, self.placements, self.shape)
 
     def redistribute_like(self, other: "DTensor") -> "DTensor":

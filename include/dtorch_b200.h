@@ -147,6 +147,16 @@ int dt_reduce_scatter(dt_comm* comm, int rank, const void* in, void* out, size_t
 int dt_all_gather(dt_comm* comm, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
                   size_t inner_bytes, void* stream);
 
+/* Shard(d, s) -> Replicate for the sub-split placement (the causal load-balancing layout of context
+ * parallelism): rank r's shard [outer, lens[r], inner] is its piece of the first s + 1 rows (fronts[r] rows)
+ * followed by its piece of the rest. out is [outer, sum(lens), inner] with every rank's front part first, in
+ * rank order, then every rank's back part. Replaces ThreadGroup::AllGatherIntoVec followed by
+ * DistributeGather::GatherShardWithSubSplit (convert_kernel.cc:164-166,
+ * distributed_scather_and_gather.cc:147-183) -- a gather and two concatenations -- with one launch of peer
+ * stores straight into place. */
+int dt_all_gather_sub_split(dt_comm* comm, int rank, const void* in, void* out, size_t outer, const int64_t* lens,
+                            const int64_t* fronts, size_t inner_bytes, void* stream);
+
 /* Shard(src_dim) -> Shard(dst_dim). `in` is this rank's contiguous local tensor of shape in_shape[0..ndim-1]
  * (in_shape[src_dim] == src_lens[rank]); src_lens[r] is rank r's extent along src_dim. The dst_dim extent D is
  * split with the reference's rule (first D % n ranks get one more), chunk k goes to rank k, and `out` is
@@ -183,6 +193,17 @@ int dt_all_gather_list(dt_comm* comm, int rank, const void* in, size_t in_bytes,
 
 /* Device-side barrier of all ranks on their streams. Replaces ThreadGroup::Barrier (thread_group.cc:118-125). */
 int dt_barrier(dt_comm* comm, int rank, void* stream);
+
+/* ---- point-to-point ----------------------------------------------------------------------------------- */
+
+/* Copy `bytes` from src (on src_device) to dst (on dst_device) with a kernel on src_device that stores straight
+ * into the destination GPU's memory over NVLink (peer access between the two devices is enabled on first use).
+ * `stream` belongs to src_device; the copy is ordered after earlier work on it and complete when it gets past
+ * the call -- a consumer on the destination device must wait for that (e.g. an event). Replaces the tensor-store
+ * hand-off of a mesh-to-mesh move, ConvertKernel::ConvertDeviceMesh (convert_kernel.cc:79-102) ->
+ * TensorStore::DestGetAndToDevice (tensor_store.cc:40-62), and the per-device pieces of gathering a DTensor onto
+ * one GPU. src_device == dst_device is a local copy. */
+int dt_peer_copy(void* dst, int dst_device, const void* src, int src_device, size_t bytes, void* stream);
 
 /* ---- NVLS buffer (NVLink SHARP) ------------------------------------------------------------------------- */
 /* Memory of every rank bound to one NVLink multicast object, so an all-reduce can reduce inside the NVSwitch

@@ -648,3 +648,63 @@ def test_list_form_rejects_oversized_sends_on_every_rank():
         assert errs == [capi.DT_ERR_INVALID] * n
     finally:
         comm.destroy()
+
+
+@pytest.mark.parametrize("mode", ["same", "peer"])
+def test_all_to_all_multi_one_launch(mode):
+    """The q/k/v swap of Ulysses attention as dt_all_to_all_multi: one kernel for the three tensors (same-device
+    mode included), equal to three dt_all_to_all calls, bit for bit."""
+    n = 8 if mode == "same" else min(ngpu(), 8)
+    if n < 2:
+        pytest.skip("peer mode needs >= 2 GPUs")
+    devs = devices_for(n, mode)
+    S, H, D = 64, 20, 16  # (1, S, H, D) Shard(1) -> Shard(2), uneven heads at n = 8
+    lens = shard_sizes(S, n)
+    g = torch.Generator().manual_seed(99)
+    host = [[torch.randn(1, lens[r], H, D, generator=g).to(torch.bfloat16) for r in range(n)] for _ in range(3)]
+    split = shard_sizes(H, n)
+    comm = capi.Comm(devs)
+    try:
+        comm.set_timeout_ms(20000)
+        d_in = [[h.to(f"cuda:{devs[r]}") for r, h in enumerate(t)] for t in host]
+        fused = [[torch.empty(1, S, split[r], D, dtype=torch.bfloat16, device=f"cuda:{devs[r]}") for r in range(n)]
+                 for _ in range(3)]
+        sep = [[torch.empty_like(o) for o in f] for f in fused]
+        counts = {}
+        import threading
+
+        bar = threading.Barrier(n)
+
+        def fn(r):
+            with torch.cuda.device(devs[r]):
+                st = torch.cuda.current_stream(devs[r])
+                s = st.cuda_stream
+                st.synchronize()
+                bar.wait(timeout=60)
+                if r == 0:
+                    counts["a"] = capi.launch_count()
+                bar.wait(timeout=60)
+                comm.all_to_all_multi(r, [d_in[t][r].data_ptr() for t in range(3)],
+                                      [fused[t][r].data_ptr() for t in range(3)], [1, lens[r], H, D], 1, 2, lens, 2, s)
+                st.synchronize()
+                bar.wait(timeout=60)
+                if r == 0:
+                    counts["b"] = capi.launch_count()
+                bar.wait(timeout=60)
+                for t in range(3):
+                    comm.all_to_all(r, d_in[t][r].data_ptr(), sep[t][r].data_ptr(), [1, lens[r], H, D], 1, 2, lens, 2, s)
+                st.synchronize()
+
+        run_ranks(n, fn)
+        for t in range(3):
+            for r in range(n):
+                assert torch.equal(fused[t][r].cpu(), sep[t][r].cpu()), (t, r)
+            full = torch.cat(host[t], dim=1)
+            for r in range(n):
+                off = sum(split[:r])
+                assert torch.equal(fused[t][r].cpu(), full[:, :, off:off + split[r]])
+        launched = counts["b"] - counts["a"]
+        # same-device: rank 0 launches the one fused kernel for the group; peer mode: one per rank
+        assert launched == (1 if mode == "same" else n), launched
+    finally:
+        comm.destroy()

@@ -390,3 +390,45 @@ def test_redistribute_by_dim_name_like_reference(mode, mesh_shape):
     assert torch.equal(y.to_torch(), full)
     cp = dtb.Shard(1) if mesh_shape[1] > 1 else dtb.Replicate()
     assert y.placements == [dtb.Shard(0), cp, dtb.Shard(1)]
+
+
+def test_mesh_move_between_two_gpus_by_peer_copy_kernel(mode):
+    # mesh [0, 1] -> mesh [1, 0]: every local crosses to the other GPU (same-device mode: stays on cuda:0)
+    need(mode, 2)
+    from dtorch_b200 import capi
+
+    a = dtb.DeviceMesh("cuda", [0, 1])
+    b = dtb.DeviceMesh("cuda", [1, 0])
+    g = torch.Generator().manual_seed(21)
+    full = torch.randn(9, 1000 + 3, generator=g).to(torch.bfloat16)  # odd rows: 4-byte-aligned runs
+    x = dtb.DTensor.from_torch(full, a, [dtb.Shard(0)])
+    n0 = capi.launch_count()
+    y = x.redistribute(device_mesh=b)
+    for d in range(min(2, ngpu())):
+        torch.cuda.synchronize(d)
+    if mode == "peer":
+        assert capi.launch_count() - n0 == 2, "one peer-copy kernel per local"
+    assert torch.equal(y.to_torch(), full)
+    assert torch.equal(y.local(1).cpu(), x.local(0).cpu()) and torch.equal(y.local(0).cpu(), x.local(1).cpu())
+    # a whole DTensor gathered onto one GPU
+    tgt = 1 if mode == "peer" else 0
+    on_gpu = x.to_torch(device=f"cuda:{tgt}")
+    assert on_gpu.device.index == tgt
+    assert torch.equal(on_gpu.cpu(), full)
+
+
+@pytest.mark.parametrize("nbytes,src_off,dst_off", [(1, 0, 0), (4097, 3, 5), ((64 << 20) + 16, 0, 0), (1000003, 16, 48)])
+def test_peer_copy_c_abi(nbytes, src_off, dst_off):
+    if ngpu() < 2:
+        pytest.skip("needs 2 GPUs")
+    from dtorch_b200 import capi
+
+    src = torch.randint(0, 255, (nbytes + src_off,), dtype=torch.uint8, device="cuda:0")
+    dst = torch.zeros(nbytes + dst_off + 7, dtype=torch.uint8, device="cuda:1")
+    s = torch.cuda.current_stream(0)
+    s.wait_stream(torch.cuda.current_stream(1))
+    capi.peer_copy(dst.data_ptr() + dst_off, 1, src.data_ptr() + src_off, 0, nbytes, s.cuda_stream)
+    s.synchronize()
+    got = dst.cpu()
+    assert torch.equal(got[dst_off:dst_off + nbytes], src.cpu()[src_off:])
+    assert int(got[:dst_off].sum()) == 0 and int(got[dst_off + nbytes:].sum()) == 0
