@@ -848,6 +848,26 @@ int common_checks(dt_comm* c, int rank) {
     return DT_OK;
 }
 
+// Local reduce-scatter in one launch: inputs of n * out_count elements, chunk k of the rank-order sum into
+// outs[k].
+int local_reduce_scatter(int n, const char* const* ins, char* const* outs, size_t out_count, int dtype, int flags,
+                         cudaStream_t stream, int dev, int num_sms) {
+    ReduceArgs a{};
+    const int pv = 16 / elem_bytes(dtype);
+    bool vec_ok = static_cast<int64_t>(out_count) % pv == 0;
+    for (int r = 0; r < n; ++r) {
+        a.in[r] = ins[r];
+        a.out[r] = outs[r];
+        vec_ok = vec_ok && aligned16(ins[r]) && aligned16(outs[r]);
+    }
+    a.n = n;
+    a.nout = 0;
+    a.out_shift = 0;
+    a.chunk = static_cast<int64_t>(out_count);
+    set_ranges(a, 0, static_cast<int64_t>(out_count) * n, pv, vec_ok);
+    return launch_reduce<false>(a, dtype, (flags & DT_ACCUM_STORAGE) != 0, dev, num_sms, stream);
+}
+
 // Local (single-device) reduce with `nout` outputs, elements [0, count).
 int local_reduce(int n, const char* const* ins, char* const* outs, int nout, size_t count, int dtype, int flags,
                  cudaStream_t stream, int dev, int num_sms) {
@@ -1262,15 +1282,12 @@ int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t ou
         return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
             if (out_count == 0) return DT_OK;
             const char* ins[kMaxRanks];
-            for (int r = 0; r < c->n; ++r) ins[r] = static_cast<const char*>(all[r].in);
-            for (int k = 0; k < c->n; ++k) {
-                const char* shifted[kMaxRanks];
-                for (int r = 0; r < c->n; ++r) shifted[r] = ins[r] + static_cast<size_t>(k) * out_count * es;
-                char* o = static_cast<char*>(all[k].out);
-                int rc = local_reduce(c->n, shifted, &o, 1, out_count, dtype, flags, st0, s.dev, s.num_sms);
-                if (rc != DT_OK) return rc;
+            char* outs[kMaxRanks];
+            for (int r = 0; r < c->n; ++r) {
+                ins[r] = static_cast<const char*>(all[r].in);
+                outs[r] = static_cast<char*>(all[r].out);
             }
-            return DT_OK;
+            return local_reduce_scatter(c->n, ins, outs, out_count, dtype, flags, st0, s.dev, s.num_sms);
         });
     }
     DT_CUDA(cudaSetDevice(s.dev));
@@ -2067,14 +2084,13 @@ int dt_local_reduce_scatter(int n, const void* const* ins, void* const* outs, si
     int dev = 0, sms = 0;
     int st = current_device_sms(&dev, &sms);
     if (st != DT_OK) return st;
-    for (int k = 0; k < n; ++k) {
-        const char* shifted[kMaxRanks];
-        for (int r = 0; r < n; ++r) shifted[r] = static_cast<const char*>(ins[r]) + static_cast<size_t>(k) * out_count * es;
-        char* o = static_cast<char*>(outs[k]);
-        st = local_reduce(n, shifted, &o, 1, out_count, dtype, flags, static_cast<cudaStream_t>(stream), dev, sms);
-        if (st != DT_OK) return st;
+    const char* in_c[kMaxRanks];
+    char* out_c[kMaxRanks];
+    for (int r = 0; r < n; ++r) {
+        in_c[r] = static_cast<const char*>(ins[r]);
+        out_c[r] = static_cast<char*>(outs[r]);
     }
-    return DT_OK;
+    return local_reduce_scatter(n, in_c, out_c, out_count, dtype, flags, static_cast<cudaStream_t>(stream), dev, sms);
 }
 
 int dt_local_all_gather(int n, const void* const* ins, void* out, size_t outer, const int64_t* lens, size_t inner_bytes,

@@ -209,6 +209,8 @@ struct ReduceArgs {
     int64_t vlo, vhi;     // 16-byte vector range of the input this launch reduces
     int64_t slo, shi;     // element range reduced one element at a time (misaligned buffers, tails)
     int64_t out_shift;    // output element index = input element index - out_shift
+    int64_t chunk;        // > 0: scatter mode -- element i goes to out[i / chunk] at i % chunk (elements; a
+                          // multiple of the vector width when vectors are used), nout unused
     int n;                // number of inputs
     int nout;             // number of outputs
 };
@@ -250,7 +252,13 @@ __device__ __forceinline__ void reduce_vectors(const ReduceArgs& a) {
                     }
                 }
                 const uint4 o = E::pack(acc);
-                for (int j = 0; j < a.nout; ++j) reinterpret_cast<uint4*>(a.out[j])[v - vshift] = o;
+                if (a.chunk > 0) {
+                    const int64_t cv = a.chunk / P;
+                    const int64_t k = v / cv;
+                    reinterpret_cast<uint4*>(a.out[k])[v - k * cv] = o;
+                } else {
+                    for (int j = 0; j < a.nout; ++j) reinterpret_cast<uint4*>(a.out[j])[v - vshift] = o;
+                }
             }
         }
     }
@@ -266,7 +274,12 @@ __device__ __forceinline__ void reduce_scalars(const ReduceArgs& a) {
             const float t = E::load1(a.in[r] + i * E::kBytes);
             acc = STORAGE ? E::round_storage(acc + t) : acc + t;
         }
-        for (int j = 0; j < a.nout; ++j) E::store1(a.out[j] + (i - a.out_shift) * E::kBytes, acc);
+        if (a.chunk > 0) {
+            const int64_t k = i / a.chunk;
+            E::store1(a.out[k] + (i - k * a.chunk) * E::kBytes, acc);
+        } else {
+            for (int j = 0; j < a.nout; ++j) E::store1(a.out[j] + (i - a.out_shift) * E::kBytes, acc);
+        }
     }
 }
 
