@@ -728,7 +728,7 @@ def run_api_leg(op, cfg, n, steps, warmup):
             torch.cuda.synchronize(d)
         ms = max(ev[d][0].elapsed_time(ev[d][1]) for d in devs) / steps
         out_in_pool = all(dtb.dtensor._host.in_pool(devs, d, y.local(d)) for d in devs)
-        nvls = bool(info["nvls"]) and op == "all_reduce" and n >= 4 and msg >= (16 << 20 if n < 6 else 8 << 20)
+        nvls = bool(info["nvls"]) and op == "all_reduce" and n >= 6 and msg >= (8 << 20)
         par = Parity(dtype, tolerance=nvls)
         if op == "all_reduce":
             want = R.fold_sum(host, code, storage_round=False)
@@ -831,14 +831,14 @@ def run_ours_multi(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     code = capi.dtype_code(dtype) if dtype in (torch.float32, torch.bfloat16, torch.float16) else 0
     # all-reduce: the two-shot P2P kernel (rank-order fold) on the heap buffers, and -- where the switch
-    # supports it and it is faster (n >= 4) -- the NVLS kernel on buffers bound to a multicast object
+    # supports it and it is faster (n >= 6) -- the NVLS kernel on buffers bound to a multicast object
     algo = {"all_reduce": "p2p two-shot (rank-order fp32 fold)",
             "reduce_scatter": "p2p pull-reduce (rank-order fp32 fold)",
             "all_gather": "p2p push (peer stores at the concat offset)",
             "all_to_all": "p2p push (pack fused into the peer stores)"}[op]
     ar_flags = 0
     xp, yp = x, y
-    if op == "all_reduce" and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
+    if op == "all_reduce" and args.algo != "p2p" and (n >= 6 or args.algo == "nvls"):
         if setup_nvls(comm, 2 * in_bytes):
             nb, _ = comm.nvls_buffer(rank)
             xn = heap_tensor(nb, 0, in_numel, dtype, dev)
@@ -1054,7 +1054,7 @@ def run_sweep_multi(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     ops = args.sweep_ops.split(",")
     nvls_base = 0
-    if "all_reduce" in ops and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):
+    if "all_reduce" in ops and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):  # sweep: compare at 4 too
         if setup_nvls(comm, 2 * max_bytes + (4 << 20)):
             nvls_base, _ = comm.nvls_buffer(rank)
     for op in ops:
@@ -1225,7 +1225,7 @@ def main():
     p.add_argument("--skip-e2e", action="store_true", help="omit the end-to-end leg (profiling runs)")
     p.add_argument("--skip-api", action="store_true", help="N > 1: omit the single-process DTensor API leg")
     p.add_argument("--algo", choices=["auto", "p2p", "nvls"], default="auto",
-                   help="all-reduce algorithm at N > 1: auto = NVLS where supported and n >= 4, else P2P two-shot")
+                   help="all-reduce algorithm at N > 1: auto = NVLS where supported and n >= 6, else P2P two-shot")
     p.add_argument("--sweep", action="store_true", help="C5 message-size sweep, one JSON line per point")
     p.add_argument("--sweep-lo", type=int, default=10, help="smallest size, log2 bytes")
     p.add_argument("--sweep-hi", type=int, default=30, help="largest size, log2 bytes")

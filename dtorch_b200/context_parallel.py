@@ -15,6 +15,11 @@ plain Shard(2) for the call and the output is viewed back (scaled_dot_product_at
 as the reference's SdpaOp::Compute does (scaled_dot_product_attention_op.cc:104-109): for a local query chunk
 shorter than the gathered key sequence that is torch's top-left aligned mask.
 
+`ulysses_overlap_groups=G` (batch 1, one q/k/v shape) pipelines the Ulysses path over G head groups: the
+executor runs each group's q/k/v swap and swap back on its kernel streams without making the caller's streams
+wait, and each device's attention of group g waits only for group g's swap, so swaps of neighbouring groups run
+while group g attends. Results equal the plain path's bit for bit.
+
 `ring_overlap=True` (non-causal, no dropout) overlaps the K/V all-gather with attention: each device attends
 its query chunk to its own key/value chunk on a side stream while the all-gather runs, then to the other
 devices' chunks, and merges the partial outputs by their log-sum-exp (softmax over the union of the chunks).
@@ -106,11 +111,89 @@ def _ring_attention_overlapped(query: DTensor, key: DTensor, value: DTensor, r: 
     return out
 
 
+class _KernelStreams:
+    """The executor's kernel stream of every device, and events that mark how far a collective enqueued there
+    has got."""
+
+    def __init__(self, ids):
+        self.streams = {}
+        for gid in ids:
+            ptr, dev = _host.kernel_stream(gid)
+            self.streams[gid] = torch.cuda.ExternalStream(ptr, device=torch.device("cuda", dev))
+
+    def mark(self):
+        evs = {}
+        for gid, s in self.streams.items():
+            e = torch.cuda.Event()
+            e.record(s)
+            evs[gid] = e
+        return evs
+
+
+def _ulysses_overlapped(query: DTensor, key: DTensor, value: DTensor, u: int, groups: int, dropout_p: float,
+                        is_causal: bool, scale: Optional[float]) -> DTensor:
+    """Ulysses attention pipelined over `groups` head groups. The executor runs the collectives on its kernel
+    streams without making the caller's streams wait (deferred hand-off); the caller's stream of each device
+    waits for a group's q/k/v swap only right before that group's attention. So the swap of group g + 1 and the
+    swap back of group g - 1 run while group g attends. Each group's heads split over the ranks as in the plain
+    path and attention is independent per head: the result equals the plain path's bit for bit."""
+    mesh = query.device_mesh
+    seq = list(query.placements)
+    head = list(seq)
+    head[u] = Shard(1)
+    H, hg = query.shape[1], query.shape[1] // groups
+    ks = _KernelStreams(mesh.ids)
+    mesh_shape, ids = list(mesh.shape), mesh.ids
+    src_p, head_p = [repr(p) for p in seq], [repr(p) for p in head]
+
+    def swap(g):
+        lo, hi = g * hg, (g + 1) * hg
+        parts = [{gid: t.local(gid)[:, lo:hi] for gid in ids} for t in (query, key, value)]
+        shape = [query.shape[0], hg] + list(query.shape[2:])
+        outs = _host.redistribute_multi(parts, mesh_shape, ids, src_p, head_p, shape, handoff=False)
+        return outs, ks.mark()
+
+    pending = swap(0)
+    backs = []
+    for g in range(groups):
+        nxt = swap(g + 1) if g + 1 < groups else None  # enqueued before this group's attention
+        (qs, kk, vs), ready = pending
+        att = {}
+        for gid in ids:
+            dev = qs[gid].device
+            with torch.cuda.device(dev):
+                cur = torch.cuda.current_stream(dev)
+                cur.wait_event(ready[gid])
+                for t in (qs[gid], kk[gid], vs[gid]):
+                    t.record_stream(cur)
+                att[gid] = F.scaled_dot_product_attention(qs[gid], kk[gid], vs[gid], dropout_p=dropout_p,
+                                                          is_causal=is_causal, scale=scale)
+        shape = [query.shape[0], hg, query.shape[2], value.shape[3]]
+        back = _host.redistribute(att, mesh_shape, ids, head_p, src_p, shape, handoff=False)
+        backs.append((back, ks.mark()))
+        pending = nxt
+    # every group's output back in sequence-sharded layout, concatenated along the heads on the caller's stream
+    out_locals = {}
+    for gid in ids:
+        dev = query.local(gid).device
+        with torch.cuda.device(dev):
+            cur = torch.cuda.current_stream(dev)
+            pieces = []
+            for back, done in backs:
+                cur.wait_event(done[gid])
+                back[gid].record_stream(cur)
+                pieces.append(back[gid])
+            out_locals[gid] = torch.cat(pieces, dim=1)
+    return DTensor(out_locals, mesh, seq, tuple(query.shape[:3]) + (value.shape[3],))
+
+
 def scaled_dot_product_attention_with_cp(query: DTensor, key: DTensor, value: DTensor, dropout_p: float = 0.0,
                                          is_causal: bool = False, scale: Optional[float] = None,
                                          ulysses_cp_dim: Optional[Union[int, str]] = None,
                                          ring_cp_dim: Optional[Union[int, str]] = None,
-                                         ring_overlap: bool = False) -> DTensor:
+                                         ring_overlap: bool = False, ulysses_overlap_groups: int = 1) -> DTensor:
+    """`ulysses_overlap_groups` > 1 pipelines a pure-Ulysses call over that many head groups (batch 1, q/k/v of
+    one shape, heads divisible by groups * Ulysses size): swaps of one group overlap attention of another."""
     u = _dim_index(query, ulysses_cp_dim)
     r = _dim_index(query, ring_cp_dim)
     if ring_overlap and (r is None or is_causal or dropout_p > 0.0):
@@ -127,6 +210,14 @@ def scaled_dot_product_attention_with_cp(query: DTensor, key: DTensor, value: DT
             raise ValueError("context-parallel dims must shard the sequence dim (Shard(2))")
     mesh = query.device_mesh
     placements = list(query.placements)
+    if u is not None and r is None and ulysses_overlap_groups > 1:
+        n = mesh.shape[u]
+        if not (query.shape == key.shape == value.shape and query.shape[0] == 1
+                and query.shape[1] % (ulysses_overlap_groups * n) == 0):
+            raise ValueError("ulysses_overlap_groups needs q, k, v of one shape, batch 1 and heads divisible by "
+                             "groups x Ulysses size")
+        out = _ulysses_overlapped(query, key, value, u, ulysses_overlap_groups, dropout_p, is_causal, scale)
+        return out if is_causal else out.view(old_placements)
     if u is not None:
         n = mesh.shape[u]
         if query.shape[1] % n or key.shape[1] % n:

@@ -1189,11 +1189,12 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
         if (want_nvls && storage)
             return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NVLS reduces in the switch with fp32 accumulation; "
                                             "DT_ACCUM_STORAGE is not available with it");
-        // measured: NVLS ahead of the two-shot kernel from 8-16 MiB at 8 ranks and from 16 MiB at 4 ranks;
-        // behind it at 2 ranks (it moves (1+1/n)S per GPU against the two-shot's 2(n-1)/n S)
-        const size_t nvls_min = c->n >= 6 ? (static_cast<size_t>(8) << 20) : (static_cast<size_t>(16) << 20);
+        // measured: at 8 ranks NVLS is ahead of the two-shot kernel from 8-16 MiB (781 vs 633 GB/s at 128 MiB);
+        // at 4 ranks the two are level within 2 % either way from 16 MiB to 1 GiB (128 MiB: 645 vs 653), so
+        // the rank-order fold stays; at 2 ranks NVLS is behind (it moves (1+1/n)S per GPU against 2(n-1)/n S)
+        const size_t nvls_min = static_cast<size_t>(8) << 20;
         const bool auto_nvls = (flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT | DT_ALGO_NVLS)) == 0 && nvls_ok && !storage &&
-                               c->n >= 4 && bytes >= nvls_min;
+                               c->n >= 6 && bytes >= nvls_min;
         if (want_nvls || auto_nvls) {
             NvlsArgs na{};
             na.sig = make_sig(c, rank);

@@ -112,18 +112,25 @@ PYBIND11_MODULE(_host, m) {
     m.def("redistribute",
           [](const std::map<int64_t, torch::Tensor>& locals, const std::vector<int64_t>& meshShape,
              const std::vector<int64_t>& meshIds, const std::vector<std::string>& src, const std::vector<std::string>& dst,
-             const std::vector<int64_t>& globalShape) {
-              return Redistribute(locals, Mesh(meshShape, meshIds), ParseSeq(src), ParseSeq(dst), globalShape);
+             const std::vector<int64_t>& globalShape, bool handoff) {
+              return Redistribute(locals, Mesh(meshShape, meshIds), ParseSeq(src), ParseSeq(dst), globalShape, handoff);
           },
-          py::call_guard<py::gil_scoped_release>());
+          py::arg("locals"), py::arg("mesh_shape"), py::arg("mesh_ids"), py::arg("src"), py::arg("dst"),
+          py::arg("global_shape"), py::arg("handoff") = true, py::call_guard<py::gil_scoped_release>());
 
     m.def("redistribute_multi",
           [](const std::vector<std::map<int64_t, torch::Tensor>>& locals, const std::vector<int64_t>& meshShape,
              const std::vector<int64_t>& meshIds, const std::vector<std::string>& src, const std::vector<std::string>& dst,
-             const std::vector<int64_t>& globalShape) {
-              return RedistributeMulti(locals, Mesh(meshShape, meshIds), ParseSeq(src), ParseSeq(dst), globalShape);
+             const std::vector<int64_t>& globalShape, bool handoff) {
+              return RedistributeMulti(locals, Mesh(meshShape, meshIds), ParseSeq(src), ParseSeq(dst), globalShape,
+                                       handoff);
           },
-          py::call_guard<py::gil_scoped_release>());
+          py::arg("locals"), py::arg("mesh_shape"), py::arg("mesh_ids"), py::arg("src"), py::arg("dst"),
+          py::arg("global_shape"), py::arg("handoff") = true, py::call_guard<py::gil_scoped_release>());
+    m.def("kernel_stream", [](int64_t globalDeviceId) {
+        auto& ks = KernelStreamManager::Global().Get(globalDeviceId);
+        return py::make_tuple(reinterpret_cast<uintptr_t>(ks.Stream().stream()), ks.CudaDevice());
+    }, "(cudaStream_t as int, CUDA device) of the kernel stream the executor runs a device's collectives on");
 
     // placement algebra (host logic; testable without a GPU)
     m.def("shard_sizes", &ShardSizes);

@@ -5,14 +5,63 @@
 #include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <algorithm>
+#include <chrono>
 #include <cstdlib>
 #include <stdexcept>
+#include <thread>
 
 namespace dtb {
 
 // ---------------------------------------------------------------------------------------------------------
 // KernelStream
 // ---------------------------------------------------------------------------------------------------------
+namespace {
+
+// How long an idle kernel-stream thread, or a poster waiting for its tasks, spins before sleeping:
+// DTORCH_B200_SPIN_US, default 2000 us (a redistribute posts its next tasks well within that).
+int64_t SpinNs() {
+    static const int64_t v = [] {
+        const char* s = std::getenv("DTORCH_B200_SPIN_US");
+        const long long us = (s != nullptr && *s != '\0') ? std::atoll(s) : 2000;
+        return static_cast<int64_t>(std::max<long long>(us, 0)) * 1000;
+    }();
+    return v;
+}
+
+inline void CpuRelax() {
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_ia32_pause();
+#else
+    std::this_thread::yield();
+#endif
+}
+
+}  // namespace
+
+void TaskBatch::Done(std::exception_ptr e) {
+    if (e) {
+        std::lock_guard<std::mutex> lock(mMutex);
+        if (!mErr) mErr = e;
+    }
+    mLeft.fetch_sub(1, std::memory_order_acq_rel);
+}
+
+void TaskBatch::Wait() {
+    const auto t0 = std::chrono::steady_clock::now();
+    uint32_t spins = 0;
+    while (mLeft.load(std::memory_order_acquire) > 0) {
+        if ((++spins & 255u) == 0 &&
+            std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count() > SpinNs()) {
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
+        } else {
+            CpuRelax();
+        }
+    }
+    std::lock_guard<std::mutex> lock(mMutex);
+    if (mErr) std::rethrow_exception(mErr);
+}
+
 KernelStream::KernelStream(int64_t globalDeviceId, int cudaDevice)
     : mGlobalDeviceId(globalDeviceId),
       mCudaDevice(cudaDevice),
@@ -29,31 +78,55 @@ KernelStream::~KernelStream() {
     if (mThread.joinable()) mThread.join();
 }
 
-std::future<void> KernelStream::Launch(std::function<void()> task) {
-    std::packaged_task<void()> pt(std::move(task));
-    auto fut = pt.get_future();
+void KernelStream::Post(std::function<void()> task, TaskBatch* batch, c10::optional<c10::cuda::CUDAStream> stream) {
+    bool wake = false;
     {
         std::lock_guard<std::mutex> lock(mMutex);
         if (mStop) throw std::runtime_error("KernelStream is shutting down");
-        mQueue.push_back(std::move(pt));
+        mQueue.push_back(Item{std::move(task), batch, stream});
+        mPending.fetch_add(1, std::memory_order_release);
+        wake = mSleeping;
     }
-    mCv.notify_one();
-    return fut;
+    if (wake) mCv.notify_one();
 }
 
 void KernelStream::Main() {
     c10::cuda::CUDAGuard device_guard(static_cast<c10::DeviceIndex>(mCudaDevice));
     c10::cuda::CUDAStreamGuard stream_guard(mStream);
     while (true) {
-        std::packaged_task<void()> task;
+        // spin a while for the next task (a redistribute posts one per mesh dim in quick succession), then sleep
+        const auto t0 = std::chrono::steady_clock::now();
+        uint32_t spins = 0;
+        while (mPending.load(std::memory_order_acquire) == 0) {
+            if ((++spins & 255u) == 0 &&
+                std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count() >
+                    SpinNs())
+                break;
+            CpuRelax();
+        }
+        Item item;
         {
             std::unique_lock<std::mutex> lock(mMutex);
+            mSleeping = true;
             mCv.wait(lock, [&] { return mStop || !mQueue.empty(); });
+            mSleeping = false;
             if (mQueue.empty()) return;  // stopping and drained
-            task = std::move(mQueue.front());
+            item = std::move(mQueue.front());
             mQueue.pop_front();
+            mPending.fetch_sub(1, std::memory_order_relaxed);
         }
-        task();  // exceptions land in the future
+        std::exception_ptr err;
+        try {
+            if (item.stream) {
+                c10::cuda::CUDAStreamGuard g(*item.stream);
+                item.fn();
+            } else {
+                item.fn();
+            }
+        } catch (...) {
+            err = std::current_exception();
+        }
+        if (item.batch != nullptr) item.batch->Done(err);
     }
 }
 
@@ -110,8 +183,47 @@ torch::Tensor ConvertPlacements(const torch::Tensor& input, const DeviceMesh& me
 // ---------------------------------------------------------------------------------------------------------
 // Redistribute
 // ---------------------------------------------------------------------------------------------------------
+namespace {
+
+// Where each device's part of a redistribute runs. handoff (the default): on the caller's current stream of that
+// device, so results are stream-ordered for the caller with no events at all. Otherwise on the device's own
+// kernel stream, ordered after the caller's work by an event and not handed back.
+struct StreamPlan {
+    bool onCaller;
+    std::map<int64_t, c10::cuda::CUDAStream> caller;
+    std::map<int64_t, std::shared_ptr<at::cuda::CUDAEvent>> ready;
+
+    StreamPlan(const DeviceMesh& mesh, bool handoff) : onCaller(handoff) {
+        for (auto id : mesh.ids) {
+            auto& ks = KernelStreamManager::Global().Get(id);
+            auto cs = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice()));
+            caller.emplace(id, cs);
+            if (!onCaller) {
+                auto ev = std::make_shared<at::cuda::CUDAEvent>();
+                ev->record(cs);
+                ready[id] = ev;
+            }
+        }
+    }
+    c10::optional<c10::cuda::CUDAStream> StreamFor(int64_t id) const {
+        if (onCaller) return caller.at(id);
+        return c10::nullopt;
+    }
+    // first task on a kernel stream: wait for the caller's work; inputs consumed on that stream stay alive
+    void Enter(int64_t id, bool first, const std::vector<torch::Tensor>& ins) const {
+        if (onCaller) return;
+        auto stream = c10::cuda::getCurrentCUDAStream();
+        if (first) ready.at(id)->block(stream);
+        for (const auto& in : ins)
+            if (in.defined() && in.is_cuda()) c10::cuda::CUDACachingAllocator::recordStream(in.storage().data_ptr(), stream);
+    }
+};
+
+}  // namespace
+
 std::map<int64_t, torch::Tensor> Redistribute(const std::map<int64_t, torch::Tensor>& locals, const DeviceMesh& mesh,
-                                              PlacementSeq src, PlacementSeq dst, const std::vector<int64_t>& globalShape) {
+                                              PlacementSeq src, PlacementSeq dst, const std::vector<int64_t>& globalShape,
+                                              bool handoff) {
     ShardDimToPositive(src, globalShape.size());
     ShardDimToPositive(dst, globalShape.size());
     ToReplicateWhenDimSizeEqualOne(src, mesh);
@@ -120,72 +232,43 @@ std::map<int64_t, torch::Tensor> Redistribute(const std::map<int64_t, torch::Ten
     CheckValid(globalShape, mesh, dst);
     for (auto id : mesh.ids)
         TORCH_CHECK(locals.count(id) == 1, "Redistribute: no local tensor for device ", id);
-
-    // order every device's kernel stream after the work already queued on the caller's stream
-    std::map<int64_t, std::shared_ptr<at::cuda::CUDAEvent>> ready;
-    for (auto id : mesh.ids) {
-        auto& ks = KernelStreamManager::Global().Get(id);
-        auto ev = std::make_shared<at::cuda::CUDAEvent>();
-        ev->record(c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice())));
-        ready[id] = ev;
-    }
+    const auto order = GetConvertOrder(src, dst);
+    if (order.empty()) return locals;
+    const StreamPlan plan(mesh, handoff);
 
     std::map<int64_t, torch::Tensor> cur = locals;
     PlacementSeq cur_p = src;
     bool first = true;
-    for (size_t d : GetConvertOrder(src, dst)) {
+    for (size_t d : order) {
         PlacementSeq next = cur_p;
         next[d] = dst[d];
         LocalShapes operand;
         operand.shapes = ComputeLocalShapes(globalShape, mesh, cur_p);
         std::map<int64_t, torch::Tensor> out;
-        std::map<int64_t, std::future<void>> futs;
-        std::mutex out_mu;
+        for (auto id : mesh.ids) out[id] = torch::Tensor();
+        TaskBatch batch(static_cast<int>(mesh.ids.size()));
         for (auto id : mesh.ids) {
-            auto& ks = KernelStreamManager::Global().Get(id);
             torch::Tensor in = cur.at(id);
-            std::shared_ptr<at::cuda::CUDAEvent> ev = first ? ready.at(id) : nullptr;
             const Placement s = cur_p[d], t = next[d];
-            futs[id] = ks.Launch([&, in, ev, s, t, id, d]() {
-                auto stream = c10::cuda::getCurrentCUDAStream();
-                if (ev) ev->block(stream);
-                // the input is consumed on this stream; keep its memory until this stream is done with it
-                if (in.defined() && in.is_cuda()) c10::cuda::CUDACachingAllocator::recordStream(in.storage().data_ptr(), stream);
-                torch::Tensor r = ConvertPlacements(in, mesh, d, s, t, id, operand);
-                std::lock_guard<std::mutex> g(out_mu);
-                out[id] = r;
-            });
+            torch::Tensor* slot = &out[id];
+            KernelStreamManager::Global().Get(id).Post(
+                [&, in, s, t, id, d, slot, first]() {
+                    plan.Enter(id, first, {in});
+                    *slot = ConvertPlacements(in, mesh, d, s, t, id, operand);
+                },
+                &batch, plan.StreamFor(id));
         }
-        std::exception_ptr err;
-        for (auto& kv : futs) {
-            try {
-                kv.second.get();
-            } catch (...) {
-                if (!err) err = std::current_exception();
-            }
-        }
-        if (err) std::rethrow_exception(err);
+        batch.Wait();
         cur = std::move(out);
         cur_p = next;
         first = false;
-    }
-    if (first) return cur;  // nothing to convert
-    // hand the results back to the caller's stream
-    for (auto id : mesh.ids) {
-        auto& ks = KernelStreamManager::Global().Get(id);
-        auto caller = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice()));
-        at::cuda::CUDAEvent done;
-        done.record(ks.Stream());
-        done.block(caller);
-        auto& t = cur.at(id);
-        if (t.defined() && t.is_cuda()) c10::cuda::CUDACachingAllocator::recordStream(t.storage().data_ptr(), caller);
     }
     return cur;
 }
 
 std::vector<std::map<int64_t, torch::Tensor>> RedistributeMulti(const std::vector<std::map<int64_t, torch::Tensor>>& locals,
                                                                 const DeviceMesh& mesh, PlacementSeq src, PlacementSeq dst,
-                                                                const std::vector<int64_t>& globalShape) {
+                                                                const std::vector<int64_t>& globalShape, bool handoff) {
     ShardDimToPositive(src, globalShape.size());
     ShardDimToPositive(dst, globalShape.size());
     ToReplicateWhenDimSizeEqualOne(src, mesh);
@@ -195,7 +278,7 @@ std::vector<std::map<int64_t, torch::Tensor>> RedistributeMulti(const std::vecto
                        dst[diff[0]].IsShard() && !src[diff[0]].HasSubSplit() && !dst[diff[0]].HasSubSplit();
     if (!fused) {
         std::vector<std::map<int64_t, torch::Tensor>> out;
-        for (const auto& l : locals) out.push_back(Redistribute(l, mesh, src, dst, globalShape));
+        for (const auto& l : locals) out.push_back(Redistribute(l, mesh, src, dst, globalShape, handoff));
         return out;
     }
     CheckValid(globalShape, mesh, src);
@@ -203,43 +286,27 @@ std::vector<std::map<int64_t, torch::Tensor>> RedistributeMulti(const std::vecto
     const size_t d = diff[0];
     LocalShapes operand;
     operand.shapes = ComputeLocalShapes(globalShape, mesh, src);
+    const StreamPlan plan(mesh, handoff);
     std::vector<std::map<int64_t, torch::Tensor>> out(locals.size());
-    std::map<int64_t, std::future<void>> futs;
-    std::mutex out_mu;
+    std::map<int64_t, std::vector<torch::Tensor>> results;
+    for (auto id : mesh.ids) results[id] = {};
+    TaskBatch batch(static_cast<int>(mesh.ids.size()));
     for (auto id : mesh.ids) {
-        auto& ks = KernelStreamManager::Global().Get(id);
         std::vector<torch::Tensor> ins;
         for (const auto& l : locals) ins.push_back(l.at(id));
-        auto ev = std::make_shared<at::cuda::CUDAEvent>();
-        ev->record(c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice())));
-        futs[id] = ks.Launch([&, ins, ev, id]() {
-            auto stream = c10::cuda::getCurrentCUDAStream();
-            ev->block(stream);
-            for (const auto& t : ins) c10::cuda::CUDACachingAllocator::recordStream(t.storage().data_ptr(), stream);
-            const auto group = GroupDeviceIds(mesh, d, id);
-            ThreadGroup& tg = ThreadGroupManager::Global().GetThreadGroup(group, id);
-            auto r = tg.AllToAllMulti(ins, static_cast<size_t>(src[d].dim), static_cast<size_t>(dst[d].dim), operand);
-            std::lock_guard<std::mutex> g(out_mu);
-            for (size_t t = 0; t < r.size(); ++t) out[t][id] = r[t];
-        });
+        std::vector<torch::Tensor>* slot = &results[id];
+        KernelStreamManager::Global().Get(id).Post(
+            [&, ins, id, slot]() {
+                plan.Enter(id, true, ins);
+                const auto group = GroupDeviceIds(mesh, d, id);
+                ThreadGroup& tg = ThreadGroupManager::Global().GetThreadGroup(group, id);
+                *slot = tg.AllToAllMulti(ins, static_cast<size_t>(src[d].dim), static_cast<size_t>(dst[d].dim), operand);
+            },
+            &batch, plan.StreamFor(id));
     }
-    std::exception_ptr err;
-    for (auto& kv : futs) {
-        try {
-            kv.second.get();
-        } catch (...) {
-            if (!err) err = std::current_exception();
-        }
-    }
-    if (err) std::rethrow_exception(err);
-    for (auto id : mesh.ids) {
-        auto& ks = KernelStreamManager::Global().Get(id);
-        auto caller = c10::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(ks.CudaDevice()));
-        at::cuda::CUDAEvent done;
-        done.record(ks.Stream());
-        done.block(caller);
-        for (auto& o : out) c10::cuda::CUDACachingAllocator::recordStream(o.at(id).storage().data_ptr(), caller);
-    }
+    batch.Wait();
+    for (auto id : mesh.ids)
+        for (size_t t = 0; t < out.size(); ++t) out[t][id] = results[id][t];
     return out;
 }
 

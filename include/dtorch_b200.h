@@ -57,7 +57,8 @@ typedef enum dt_redop {
  *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size.
  *   DT_ALGO_NVLS      reduce inside the NVSwitch (NVLink SHARP): needs input and output in the communicator's
  *                     NVLS buffer (dt_comm_nvls_*); fp32 accumulation in the switch's order, not rank order.
- *                     Picked by default for such buffers at >= 4 ranks from 16 MiB (>= 6 ranks: 8 MiB). */
+ *                     Picked by default for such buffers at >= 6 ranks from 8 MiB (where it measured faster
+ *                     than the rank-order kernels; at 4 ranks they are level, so the rank-order fold stays). */
 #define DT_ACCUM_FP32 0x0
 #define DT_ACCUM_STORAGE 0x1
 #define DT_ALGO_AUTO 0x00

@@ -379,14 +379,16 @@ def test_nvls_all_reduce(dtype):
 
 
 def test_nvls_picked_by_default_from_switch_over_size():
+    """At >= 6 ranks an all-reduce on NVLS-buffer operands of 8 MiB or more reduces in the switch by default; at
+    4 ranks it keeps the rank-order kernel (measured level with NVLS there)."""
     n = min(ngpu(), 8)
     if n < 4:
-        pytest.skip("NVLS is the default from 4 ranks")
+        pytest.skip("needs >= 4 GPUs")
     comm = capi.Comm(list(range(n)))
     try:
         if not comm.nvls_supported():
             pytest.skip("NVLink multicast not supported here")
-        count = ((8 if n >= 6 else 16) << 20) // 2 + 64  # bf16, just above the switch-over size
+        count = (8 << 20) // 2 + 64  # bf16, just above the switch-over size
         comm.nvls_alloc(2 * count * 2 + (1 << 20))
         g = torch.Generator().manual_seed(9)
         host = [torch.randn(count, generator=g).to(torch.bfloat16) for _ in range(n)]
@@ -409,7 +411,10 @@ def test_nvls_picked_by_default_from_switch_over_size():
             outs[flags] = [np_raw(y) for y in ys]
         want = R.fold_sum([raw_from_torch(h) for h in host], DT_CODE["bfloat16"], storage_round=False)
         for r in range(n):
-            assert np.array_equal(outs[0][r], outs[capi.DT_ALGO_NVLS][r])
+            if n >= 6:
+                assert np.array_equal(outs[0][r], outs[capi.DT_ALGO_NVLS][r])
+            else:  # the rank-order fold, bit for bit
+                assert np.array_equal(outs[0][r], want)
             assert_close(outs[0][r], want, "bfloat16")
     finally:
         comm.destroy()

@@ -2,8 +2,8 @@
 
 With a pool, from_torch places every device's local at the same offset of the group's peer-mapped memory and
 every collective allocates its outputs there too, so the collectives resolve peers without the per-call
-pointer exchange; on NVLink-multicast GPUs the pool is the NVLS buffer and all-reduces of 16 MiB and more at
->= 4 ranks reduce in the switch. Results are checked against the oracle as everywhere else (bit-exact for
+pointer exchange; on NVLink-multicast GPUs the pool is the NVLS buffer and all-reduces of 8 MiB and more at
+>= 6 ranks reduce in the switch. Results are checked against the oracle as everywhere else (bit-exact for
 moves and rank-order folds; NVLS within the reductions' tolerance).
 """
 
@@ -78,8 +78,8 @@ def test_pool_collectives_stay_in_pool_and_match_oracle(pool, n):
 
 def test_pool_nvls_all_reduce_within_tolerance(pool):
     n = min(ngpu(), 8)
-    if n < 4:
-        pytest.skip("the NVLS all-reduce is chosen at >= 4 ranks")
+    if n < 6:
+        pytest.skip("the NVLS all-reduce is chosen at >= 6 ranks")
     mesh = dtb.DeviceMesh("cuda", list(range(n)))
     info = dtb.dtensor._host.pool_info(mesh.ids, 0)
     if not info["nvls"]:

@@ -432,3 +432,22 @@ def test_peer_copy_c_abi(nbytes, src_off, dst_off):
     got = dst.cpu()
     assert torch.equal(got[dst_off:dst_off + nbytes], src.cpu()[src_off:])
     assert int(got[:dst_off].sum()) == 0 and int(got[dst_off + nbytes:].sum()) == 0
+
+
+@pytest.mark.parametrize("groups", [2, 4])
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_ulysses_overlapped_equals_plain(mode, groups, is_causal):
+    n = 2
+    need(mode, n)
+    mesh = dtb.init_device_mesh("cuda", (n,), mesh_dim_names=["cp"])
+    g = torch.Generator().manual_seed(31)
+    q, k, v = (torch.randn(1, 16, 96, 64, generator=g).to(torch.bfloat16) for _ in range(3))
+    dq, dk, dv = (dtb.DTensor.from_torch(t, mesh, [dtb.Shard(2)]) for t in (q, k, v))
+    plain = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, is_causal=is_causal, ulysses_cp_dim="cp")
+    piped = dtb.scaled_dot_product_attention_with_cp(dq, dk, dv, is_causal=is_causal, ulysses_cp_dim="cp",
+                                                     ulysses_overlap_groups=groups)
+    for d in range(min(n, ngpu())):
+        torch.cuda.synchronize(d)
+    assert piped.placements == plain.placements
+    for gid in mesh.ids:
+        assert torch.equal(piped.local(gid).cpu(), plain.local(gid).cpu()), gid
