@@ -1084,9 +1084,9 @@ def run_sweep_multi(args, rank, world, local_rank):
                 def ours():
                     st = stream.cuda_stream
                     if op == "all_reduce":
-                        comm.all_reduce(rank, x.data_ptr(), y.data_ptr(), in_n, code, 0, st)
+                        comm.all_reduce(rank, x.data_ptr(), y.data_ptr(), in_n, code, args.sweep_flags, st)
                     elif op == "reduce_scatter":
-                        comm.reduce_scatter(rank, x.data_ptr(), y.data_ptr(), out_n, code, 0, st)
+                        comm.reduce_scatter(rank, x.data_ptr(), y.data_ptr(), out_n, code, args.sweep_flags, st)
                     elif op == "all_gather":
                         comm.all_gather(rank, x.data_ptr(), y.data_ptr(), 1, [in_n] * n, es, st)
                     else:
@@ -1135,6 +1135,30 @@ def run_sweep_multi(args, rank, world, local_rank):
                     tm = torch.tensor([ms], device=dev)
                     dist.all_reduce(tm, op=dist.ReduceOp.MAX)
                     res[name] = float(tm.item())
+                    if args.sweep_graph and name != "nccl":
+                        # the same calls captured once into a CUDA graph and replayed: device time without the
+                        # host's launch gaps (every rank captures and replays the same sequence)
+                        g = torch.cuda.CUDAGraph()
+                        dist.barrier()
+                        torch.cuda.synchronize()
+                        with torch.cuda.graph(g, stream=stream):
+                            for _ in range(iters):
+                                fn()
+                        torch.cuda.synchronize()
+                        dist.barrier()
+                        with torch.cuda.stream(stream):
+                            g.replay()
+                        torch.cuda.synchronize()
+                        dist.barrier()
+                        def replay():
+                            with torch.cuda.stream(stream):
+                                g.replay()
+
+                        gms = time_steps(replay, 1, stream) / iters
+                        tm = torch.tensor([gms], device=dev)
+                        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+                        res[name + "_graph"] = float(tm.item())
+                        del g
                 busf = bus_factor(op, n)
                 msg = in_n * es if op != "all_gather" else out_n * es
                 if rank == 0:
@@ -1147,6 +1171,9 @@ def run_sweep_multi(args, rank, world, local_rank):
                     if "nvls" in res:
                         line["nvls_ms"] = round(res["nvls"], 5)
                         line["nvls_bus_gbs"] = round(msg * busf / res["nvls"] / 1e6, 2)
+                    for key in [k for k in res if k.endswith("_graph")]:
+                        line[key + "_ms"] = round(res[key], 5)
+                        line[key + "_bus_gbs"] = round(msg * busf / res[key] / 1e6, 2)
                     print(json.dumps(line), flush=True)
                 del xa, ya
     dist.barrier()
@@ -1231,6 +1258,8 @@ def main():
     p.add_argument("--sweep-hi", type=int, default=30, help="largest size, log2 bytes")
     p.add_argument("--sweep-ops", default="all_reduce,all_gather,reduce_scatter,all_to_all")
     p.add_argument("--sweep-no-nccl", action="store_true", help="sweep without the NCCL comparison")
+    p.add_argument("--sweep-graph", action="store_true", help="sweep: also time our calls replayed from a CUDA graph")
+    p.add_argument("--sweep-flags", type=int, default=0, help="sweep: reduction flags of our all-reduce / reduce-scatter (e.g. 0x20 forces the two-shot kernel)")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -29,7 +29,6 @@ DT_ACCUM_STORAGE = 0x1
 DT_ALGO_ONESHOT = 0x10
 DT_ALGO_TWOSHOT = 0x20
 DT_ALGO_NVLS = 0x40
-DT_ALGO_PUSH = 0x80
 
 MAX_RANKS = 8
 

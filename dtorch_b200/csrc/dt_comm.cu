@@ -48,25 +48,9 @@ int fail(int status, const std::string& msg) {
         }                                                                                      \
     } while (0)
 
-// Slab of one rank: [barrier flags [kMaxBlocks][kMaxRanks] | epochs [kMaxBlocks] | pushed [kMaxBlocks][kMaxRanks] |
-// freed [kMaxBlocks][kMaxRanks] | rounds [kMaxBlocks] | pad to 128 KiB | staging | heap]. Every rank has the same
-// layout, so a peer's arrays are at the same offsets of its slab.
-constexpr size_t kFlagArray = static_cast<size_t>(kMaxBlocks) * kMaxRanks * sizeof(uint32_t);
-constexpr size_t kCounterArray = static_cast<size_t>(kMaxBlocks) * sizeof(uint32_t);
-constexpr size_t kPushedOffset = kFlagArray + kCounterArray;
-constexpr size_t kFreedOffset = kPushedOffset + kFlagArray;
-constexpr size_t kRoundsOffset = kFreedOffset + kFlagArray;
-constexpr size_t kFlagBytes = kRoundsOffset + kCounterArray;
-constexpr size_t kStagingOffset = 128 * 1024;
-static_assert(kFlagBytes <= kStagingOffset, "flag arrays overflow their part of the slab");
-
-// Staging of the push-based reductions (two windows per source rank), per rank, in bytes: DTORCH_B200_STAGING_MB,
-// default 128 MiB; rounded to 64 KiB. Must be equal on every rank of a communicator.
-size_t staging_bytes_default() {
-    const char* s = std::getenv("DTORCH_B200_STAGING_MB");
-    const long long mb = (s != nullptr && *s != '\0') ? std::atoll(s) : 128;
-    return static_cast<size_t>(std::max<long long>(mb, 0)) << 20;
-}
+// [kMaxBlocks][kMaxRanks] barrier flags, then kMaxBlocks per-block epoch counters
+constexpr size_t kFlagBytes = static_cast<size_t>(kMaxBlocks) * (kMaxRanks + 1) * sizeof(uint32_t);
+constexpr size_t kHeapOffset = 64 * 1024;  // heap starts 64 KiB into the slab (flags first)
 constexpr uint32_t kHandleMagic = 0x44544232u;  // "DTB2"
 
 // Restores the calling thread's current device on scope exit: the CUDA runtime shares the thread's current
@@ -99,7 +83,6 @@ struct IpcHandle {
     int32_t nranks;
     int32_t pad;
     uint64_t heap_bytes;
-    uint64_t staging_bytes;
     cudaIpcMemHandle_t mem;
 };
 
@@ -114,9 +97,7 @@ struct RankState {
     int* err = nullptr;           // host-mapped error word
     uint64_t rv_gen = 0;          // rendezvous generations passed by this rank
     cudaEvent_t ready = nullptr;  // same-device mode
-    char* staging = nullptr;               // this rank's staging (two windows per source rank)
-    uint32_t* peer_flags[kMaxRanks] = {};  // slab (flags first) of rank r as addressed from this rank's device
-    char* peer_stage[kMaxRanks] = {};      // staging of rank r as addressed from this rank's device
+    uint32_t* peer_flags[kMaxRanks] = {};  // flags of rank r as addressed from this rank's device
     char* peer_heap[kMaxRanks] = {};       // heap of rank r as addressed from this rank's device
     bool imported[kMaxRanks] = {};         // peer slab opened through IPC (must be closed)
     // NVLS buffer: this rank's memory bound to the communicator's multicast object
@@ -149,8 +130,6 @@ struct dt_comm {
     std::atomic<bool> broken{false};
     int local_rank = -1;  // multi-process: the rank this process holds
     size_t heap_bytes = 0;
-    size_t staging_bytes = 0;
-    size_t heap_offset = kStagingOffset;  // kStagingOffset + staging_bytes
     int64_t timeout_ms = 600000;
     RankState r[kMaxRanks];
     // in-process rendezvous: double-buffered slots indexed by generation parity
@@ -190,12 +169,11 @@ int alloc_rank(dt_comm* c, int rank, int dev, size_t heap_bytes) {
     s.dev = dev;
     DT_CUDA(cudaSetDevice(dev));
     DT_CUDA(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
-    const size_t bytes = c->heap_offset + heap_bytes;
+    const size_t bytes = kHeapOffset + heap_bytes;
     DT_CUDA(cudaMalloc(&s.slab, bytes));
     DT_CUDA(cudaMemset(s.slab, 0, kFlagBytes));
     s.flags = reinterpret_cast<uint32_t*>(s.slab);
-    s.staging = c->staging_bytes > 0 ? s.slab + kStagingOffset : nullptr;
-    s.heap = s.slab + c->heap_offset;
+    s.heap = s.slab + kHeapOffset;
     DT_CUDA(cudaHostAlloc(&s.err, sizeof(int) * 4, cudaHostAllocMapped | cudaHostAllocPortable));
     *reinterpret_cast<volatile int*>(s.err) = 0;
     DT_CUDA(cudaEventCreateWithFlags(&s.ready, cudaEventDisableTiming));
@@ -862,95 +840,6 @@ int launch_nvls_t(const NvlsArgs& a, int dev, int num_sms, cudaStream_t stream, 
     return launch_check("k_allreduce_nvls");
 }
 
-// ---------------------------------------------------------------------------------------------------------
-// Push-based reductions (k_push_reduce)
-// ---------------------------------------------------------------------------------------------------------
-template <int DT, int NR, bool ST>
-int launch_push_t(const PushArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want) {
-    auto k = k_push_reduce<DT, NR, ST>;
-    want = std::min(want, p2p_ctas());
-    int grid = 1;
-    pick_grid(k, dev, num_sms, want, 1, &grid);
-    k<<<grid, kThreads, 0, stream>>>(a);
-    return launch_check("k_push_reduce");
-}
-
-template <int DT, bool ST>
-int launch_push_nr(const PushArgs& a, int dev, int num_sms, cudaStream_t stream, int64_t want) {
-    if (a.sig.n <= 2) return launch_push_t<DT, 2, ST>(a, dev, num_sms, stream, want);
-    if (a.sig.n <= 4) return launch_push_t<DT, 4, ST>(a, dev, num_sms, stream, want);
-    return launch_push_t<DT, 8, ST>(a, dev, num_sms, stream, want);
-}
-
-// Whether the default picks the push-based reduce phase (DTORCH_B200_PUSH=0 turns it off); equal on every rank.
-bool push_default_on() {
-    static const bool v = [] {
-        const char* s = std::getenv("DTORCH_B200_PUSH");
-        return !(s != nullptr && std::string(s) == "0");
-    }();
-    return v;
-}
-
-// The push-based path serves messages whose chunks are whole 16-byte vectors of 16-byte aligned buffers
-// (decided from every rank's pointers, so every rank takes the same path).
-bool push_possible(const dt_comm* c, int rank, int64_t chunk_elems, int es, const char* const* ins, char* const* outs,
-                   int nout) {
-    const RankState& s = c->r[rank];
-    if (c->staging_bytes < static_cast<size_t>(2 * c->n) * 16 || s.staging == nullptr) return false;
-    if (chunk_elems <= 0 || (chunk_elems * es) % 16 != 0) return false;
-    for (int r = 0; r < c->n; ++r)
-        if (!aligned16(ins[r])) return false;
-    for (int j = 0; j < nout; ++j)
-        if (!aligned16(outs[j])) return false;
-    return true;
-}
-
-// Reduce chunk `rank` of every rank's input (each input = n chunks of chunk_elems) into this rank's output
-// (reduce-scatter, outs[0]) or into every rank's output (all-reduce, outs[k] = rank k's output).
-int push_reduce(dt_comm* c, int rank, const char* in, char* const* outs, int64_t chunk_elems, int dtype, bool storage,
-                bool allreduce, cudaStream_t stream) {
-    RankState& s = c->r[rank];
-    const int es = elem_bytes(dtype);
-    PushArgs a{};
-    a.in = in;
-    for (int k = 0; k < c->n; ++k) {
-        a.stage[k] = s.peer_stage[k];
-        a.pushed[k] = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(s.peer_flags[k]) + kPushedOffset);
-        a.freed[k] = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(s.peer_flags[k]) + kFreedOffset);
-        a.out[k] = allreduce ? outs[k] : (k == 0 ? outs[0] : nullptr);
-    }
-    a.rounds = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(s.flags) + kRoundsOffset);
-    a.sig = make_sig(c, rank);
-    a.chunk_vecs = chunk_elems * es / 16;
-    a.window_vecs = static_cast<int64_t>(c->staging_bytes / (static_cast<size_t>(2 * c->n) * 16));
-    if (a.window_vecs >= a.chunk_vecs) a.window_vecs = a.chunk_vecs;
-    a.nrounds = static_cast<int>((a.chunk_vecs + a.window_vecs - 1) / a.window_vecs);
-    a.allreduce = allreduce ? 1 : 0;
-    // grid from sizes every rank shares: one block per SM at most, fewer for small windows
-    const int64_t want = std::max<int64_t>(1, (a.window_vecs + kThreads * 2 - 1) / (kThreads * 2));
-    switch (dtype) {
-        case DT_FLOAT32: return launch_push_nr<0, false>(a, s.dev, s.num_sms, stream, want);
-        case DT_BFLOAT16:
-            return storage ? launch_push_nr<1, true>(a, s.dev, s.num_sms, stream, want)
-                           : launch_push_nr<1, false>(a, s.dev, s.num_sms, stream, want);
-        case DT_FLOAT16:
-            return storage ? launch_push_nr<2, true>(a, s.dev, s.num_sms, stream, want)
-                           : launch_push_nr<2, false>(a, s.dev, s.num_sms, stream, want);
-        default: return fail(DT_ERR_INVALID, "unsupported dtype");
-    }
-}
-
-// Push or pull reduce phase: DT_ALGO_PUSH forces push where possible, DT_ALGO_TWOSHOT forces pull; by default
-// push from kPushMinBytes of chunk per rank.
-constexpr int64_t kPushMinBytes = static_cast<int64_t>(1) << 20;
-bool use_push(const dt_comm* c, int rank, int flags, int64_t chunk_elems, int es, const char* const* ins,
-              char* const* outs, int nout) {
-    if (!push_possible(c, rank, chunk_elems, es, ins, outs, nout)) return false;
-    if (flags & DT_ALGO_PUSH) return true;
-    if (flags & (DT_ALGO_TWOSHOT | DT_ALGO_ONESHOT)) return false;
-    return push_default_on() && chunk_elems * es >= kPushMinBytes;
-}
-
 int common_checks(dt_comm* c, int rank) {
     if (c == nullptr) return fail(DT_ERR_INVALID, "null communicator");
     if (!check_rank(c, rank)) return fail(DT_ERR_INVALID, "rank out of range for this communicator");
@@ -1081,8 +970,6 @@ int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_co
     c->n = nranks;
     c->same_device = same && nranks > 1;
     c->heap_bytes = heap_bytes;
-    c->staging_bytes = (c->same_device || nranks < 2) ? 0 : staging_bytes_default() / (64 << 10) * (64 << 10);
-    c->heap_offset = kStagingOffset + c->staging_bytes;
     c->timeout_ms = env_timeout_ms();
     c->arrived[0] = 0;
     c->arrived[1] = 0;
@@ -1116,7 +1003,6 @@ int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_co
             for (int j = 0; j < nranks; ++j) {
                 c->r[i].peer_flags[j] = c->r[j].flags;
                 c->r[i].peer_heap[j] = c->r[j].heap;
-                c->r[i].peer_stage[j] = c->r[j].staging;
             }
     }
     if (st != DT_OK) {
@@ -1140,8 +1026,6 @@ int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes
     c->multiprocess = true;
     c->local_rank = rank;
     c->heap_bytes = heap_bytes;
-    c->staging_bytes = nranks < 2 ? 0 : staging_bytes_default() / (64 << 10) * (64 << 10);
-    c->heap_offset = kStagingOffset + c->staging_bytes;
     c->timeout_ms = env_timeout_ms();
     int st = alloc_rank(c, rank, cuda_device, heap_bytes);
     if (st != DT_OK) {
@@ -1152,7 +1036,6 @@ int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes
     }
     c->r[rank].peer_flags[rank] = c->r[rank].flags;
     c->r[rank].peer_heap[rank] = c->r[rank].heap;
-    c->r[rank].peer_stage[rank] = c->r[rank].staging;
     c->ready = nranks == 1;
     *out = c;
     return DT_OK;
@@ -1169,7 +1052,6 @@ int dt_comm_export(dt_comm* c, void* handle) {
     h.rank = c->local_rank;
     h.nranks = c->n;
     h.heap_bytes = c->heap_bytes;
-    h.staging_bytes = c->staging_bytes;
     DT_CUDA(cudaSetDevice(s.dev));
     DT_CUDA(cudaIpcGetMemHandle(&h.mem, s.slab));
     std::memcpy(handle, &h, sizeof(h));
@@ -1186,17 +1068,14 @@ int dt_comm_import(dt_comm* c, const void* handles) {
     for (int r = 0; r < c->n; ++r) {
         if (r == me) continue;
         const IpcHandle& h = hs[r];
-        if (h.magic != kHandleMagic || h.rank != r || h.nranks != c->n || h.heap_bytes != c->heap_bytes ||
-            h.staging_bytes != c->staging_bytes)
-            return fail(DT_ERR_INVALID, "import: handle does not match this communicator (ranks, heap or staging size "
-                                        "differ; DTORCH_B200_STAGING_MB must be equal on every rank)");
+        if (h.magic != kHandleMagic || h.rank != r || h.nranks != c->n || h.heap_bytes != c->heap_bytes)
+            return fail(DT_ERR_INVALID, "import: handle does not match this communicator");
         if (s.imported[r]) continue;
         void* p = nullptr;
         DT_CUDA(cudaIpcOpenMemHandle(&p, h.mem, cudaIpcMemLazyEnablePeerAccess));
         s.imported[r] = true;
         s.peer_flags[r] = reinterpret_cast<uint32_t*>(p);
-        s.peer_heap[r] = static_cast<char*>(p) + c->heap_offset;
-        s.peer_stage[r] = c->staging_bytes > 0 ? static_cast<char*>(p) + kStagingOffset : nullptr;
+        s.peer_heap[r] = static_cast<char*>(p) + kHeapOffset;
     }
     c->ready = true;
     return DT_OK;
@@ -1352,11 +1231,6 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
     // ranks pick the same kernel even when only some of them reduce in place
     for (int r = 0; r < c->n; ++r)
         if (ins[r] == outs[r]) algo = DT_ALGO_TWOSHOT;
-    // two-shot with the push-based reduce phase: chunk c (count / n elements, whole vectors) owned by rank c
-    if (algo == DT_ALGO_TWOSHOT && (flags & DT_ALGO_NVLS) == 0 && count % static_cast<size_t>(c->n) == 0 &&
-        use_push(c, rank, flags, static_cast<int64_t>(count / c->n), es, ins, outs, c->n))
-        return push_reduce(c, rank, static_cast<const char*>(in), outs, static_cast<int64_t>(count / c->n), dtype,
-                           storage, true, stream);
     if (algo == DT_ALGO_ONESHOT) {
         a.out[0] = outs[rank];
         a.nout = 1;
@@ -1426,11 +1300,6 @@ int dt_reduce_scatter(dt_comm* c, int rank, const void* in, void* out, size_t ou
     char* outs[kMaxRanks];
     st = resolve_peers(c, rank, in, in_count * es, out, out_count * es, ins, outs);
     if (st != DT_OK) return st;
-    if (use_push(c, rank, flags, static_cast<int64_t>(out_count), es, ins, outs, c->n)) {
-        char* own[1] = {static_cast<char*>(out)};
-        return push_reduce(c, rank, static_cast<const char*>(in), own, static_cast<int64_t>(out_count), dtype,
-                           (flags & DT_ACCUM_STORAGE) != 0, false, stream);
-    }
     ReduceArgs a{};
     a.sig = make_sig(c, rank);
     a.n = c->n;

@@ -505,153 +505,6 @@ __global__ void __launch_bounds__(kThreads) k_allreduce_nvls(const __grid_consta
     block_barrier(a.sig, 2 * e);
 }
 
-// ------------------------------------------------------------------------------------------------------------
-// Push-based reduce-scatter / all-reduce. Pulling a peer's input (the two-shot kernel's reduce phase) runs at
-// ~665-672 GB/s per direction when both directions are busy; storing to a peer runs at ~709. Here every rank
-// pushes the chunks the other ranks own into their staging memory, and each owner folds its chunk locally in
-// rank order -- the same fp32 sum, bit for bit -- then (all-reduce) pushes the result to every rank's output.
-//
-// The message is cut into rounds of one staging window; staging holds two windows per source rank, so round
-// t + 1's pushes can land while round t is being folded. Block b of every rank handles the same slice of every
-// window, so flags pair block b with block b: `pushed[b][i]` (in the owner's memory, written by source i) says
-// "round t of mine is in your staging", `freed[b][c]` (in the source's memory, written by owner c) says "I
-// have folded round t from your slot". Flag values come from a per-block round counter in device memory that
-// advances by the number of rounds on every rank alike, so flags never need resetting. Every wait is bounded
-// by the communicator timeout and ends in kErrTimeout, never a hang.
-// ------------------------------------------------------------------------------------------------------------
-struct PushArgs {
-    const char* in;                // this rank's input: n chunks of chunk_vecs 16-byte vectors
-    char* stage[kMaxRanks];        // rank k's staging (2 windows x n slots), as addressed from this GPU
-    char* out[kMaxRanks];          // all-reduce: rank k's output; reduce-scatter: out[0] = this rank's output
-    uint32_t* pushed[kMaxRanks];   // rank k's [kMaxBlocks][kMaxRanks] "round pushed" flags
-    uint32_t* freed[kMaxRanks];    // rank k's [kMaxBlocks][kMaxRanks] "slot folded" flags
-    uint32_t* rounds;              // this rank's per-block round counters
-    SignalCtx sig;
-    int64_t chunk_vecs;            // vectors per rank chunk
-    int64_t window_vecs;           // vectors per staging slot
-    int nrounds;
-    int allreduce;
-};
-
-// Threads j < n, j != rank wait until flags[j] (in this GPU's memory) reaches `value`; false on timeout.
-__device__ __forceinline__ bool wait_flags(const uint32_t* flags, const SignalCtx& s, uint32_t value) {
-    bool ok = true;
-    if (threadIdx.x < s.n && threadIdx.x != s.rank) {
-        const uint32_t* f = flags + threadIdx.x;
-        uint64_t start = 0;
-        uint32_t spins = 0;
-        while (static_cast<int32_t>(ld_acquire_sys(f) - value) < 0) {
-            if ((++spins & 31u) == 0) {
-                const uint64_t now = global_timer_ns();
-                if (start == 0) {
-                    start = now;
-                } else if (now - start > s.timeout_ns) {
-                    *reinterpret_cast<volatile int*>(s.err) = kErrTimeout;
-                    ok = false;
-                    break;
-                }
-            }
-        }
-    }
-    return __syncthreads_and(ok) != 0;
-}
-
-// After __syncthreads: tell every other rank k (thread k) `value` at slot [blockIdx.x][rank] of its array.
-__device__ __forceinline__ void announce(uint32_t* const* arrays, const SignalCtx& s, uint32_t value) {
-    __syncthreads();
-    if (threadIdx.x < s.n && threadIdx.x != s.rank)
-        st_release_sys(arrays[threadIdx.x] + blockIdx.x * kMaxRanks + s.rank, value);
-}
-
-template <int DT, int NRMAX, bool STORAGE>
-__global__ void __launch_bounds__(kThreads) k_push_reduce(const __grid_constant__ PushArgs a) {
-    using E = Elem<DT>;
-    constexpr int P = E::kPerVec;
-    constexpr int U = 2;
-    const int n = a.sig.n, r = a.sig.rank;
-    const uint32_t e = block_epoch(a.sig);
-    if (!block_barrier(a.sig, 2 * e - 1)) return;
-    __shared__ uint32_t base_s;
-    if (threadIdx.x == 0) {
-        base_s = a.rounds[blockIdx.x];
-        a.rounds[blockIdx.x] = base_s + static_cast<uint32_t>(a.nrounds);
-    }
-    __syncthreads();
-    const uint32_t base = base_s;
-    const uint4* in = reinterpret_cast<const uint4*>(a.in);
-    const uint32_t* my_pushed = a.pushed[r] + blockIdx.x * kMaxRanks;
-    const uint32_t* my_freed = a.freed[r] + blockIdx.x * kMaxRanks;
-    const int64_t step = static_cast<int64_t>(blockDim.x) * U;
-    for (int t = 0; t < a.nrounds; ++t) {
-        const int buf = t & 1;
-        const int64_t w0 = static_cast<int64_t>(t) * a.window_vecs;
-        const int64_t wv = min(a.window_vecs, a.chunk_vecs - w0);
-        const int64_t lo = wv * blockIdx.x / gridDim.x, hi = wv * (blockIdx.x + 1) / gridDim.x;
-        // slot `buf` of every destination is free again once that destination folded round t - 2
-        if (t >= 2 && !wait_flags(my_freed, a.sig, base + static_cast<uint32_t>(t) - 1)) return;
-        // push this rank's part of chunk c, window t, to rank c's slot (buf, r)
-        for (int j = 1; j < n; ++j) {
-            const int c = (r + j) % n;
-            const uint4* src = in + c * a.chunk_vecs + w0;
-            uint4* dst = reinterpret_cast<uint4*>(a.stage[c]) + (static_cast<int64_t>(buf) * n + r) * a.window_vecs;
-            for (int64_t v0 = lo + threadIdx.x; v0 < hi; v0 += step) {
-                uint4 x[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (v0 + u * blockDim.x < hi) x[u] = src[v0 + u * blockDim.x];
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (v0 + u * blockDim.x < hi) dst[v0 + u * blockDim.x] = x[u];
-            }
-        }
-        announce(a.pushed, a.sig, base + static_cast<uint32_t>(t) + 1);
-        if (!wait_flags(my_pushed, a.sig, base + static_cast<uint32_t>(t) + 1)) return;
-        // fold rank r's chunk, window t, in rank order: own input at position r, staging slots elsewhere
-        const uint4* slot[NRMAX];
-#pragma unroll
-        for (int i = 0; i < NRMAX; ++i)
-            slot[i] = i == r ? in + r * a.chunk_vecs + w0
-                             : reinterpret_cast<const uint4*>(a.stage[r]) + (static_cast<int64_t>(buf) * n + (i < n ? i : 0)) * a.window_vecs;
-        for (int64_t v0 = lo + threadIdx.x; v0 < hi; v0 += step) {
-            uint4 x[NRMAX][U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int64_t v = v0 + u * blockDim.x;
-                if (v < hi) {
-#pragma unroll
-                    for (int i = 0; i < NRMAX; ++i)
-                        if (i < n) x[i][u] = slot[i][v];
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int64_t v = v0 + u * blockDim.x;
-                if (v >= hi) continue;
-                float acc[P];
-                E::unpack(x[0][u], acc);
-#pragma unroll
-                for (int i = 1; i < NRMAX; ++i) {
-                    if (i < n) {
-                        float tt[P];
-                        E::unpack(x[i][u], tt);
-#pragma unroll
-                        for (int q = 0; q < P; ++q) acc[q] = STORAGE ? E::round_storage(acc[q] + tt[q]) : acc[q] + tt[q];
-                    }
-                }
-                const uint4 o = E::pack(acc);
-                if (a.allreduce) {
-                    const int64_t at = r * a.chunk_vecs + w0 + v;
-                    for (int j = 1; j <= n; ++j) reinterpret_cast<uint4*>(a.out[(r + j) % n])[at] = o;
-                } else {
-                    reinterpret_cast<uint4*>(a.out[0])[w0 + v] = o;
-                }
-            }
-        }
-        announce(a.freed, a.sig, base + static_cast<uint32_t>(t) + 1);
-    }
-    block_barrier(a.sig, 2 * e);
-}
-
 // Barrier-only kernel (ThreadGroup::Barrier): one block, both phases of the epoch.
 __global__ void k_barrier(const __grid_constant__ SignalCtx s) {
     const uint32_t e = block_epoch(s);

@@ -94,18 +94,21 @@ class DeviceMesh:
         self.mesh = t
         self.device_type = "cuda"
         self.dim_names = list(mesh_dim_names) if mesh_dim_names else []
+        # the mesh is immutable: its shape and ids are read on every redistribute, so keep them at hand
+        self._shape = tuple(int(x) for x in t.shape)
+        self._ids = [int(x) for x in t.reshape(-1).tolist()]
 
     @property
     def shape(self):
-        return tuple(self.mesh.shape)
+        return self._shape
 
     @property
     def ndim(self) -> int:
-        return self.mesh.dim()
+        return len(self._shape)
 
     @property
     def ids(self) -> List[int]:
-        return self.mesh.reshape(-1).tolist()
+        return list(self._ids)
 
     @property
     def is_distributed(self) -> bool:
@@ -118,7 +121,7 @@ class DeviceMesh:
         return self.dim_names.index(dim_name) if dim_name in self.dim_names else default_value
 
     def __eq__(self, other) -> bool:
-        return isinstance(other, DeviceMesh) and torch.equal(self.mesh, other.mesh)
+        return isinstance(other, DeviceMesh) and self._shape == other._shape and self._ids == other._ids
 
     def __repr__(self) -> str:
         return f"DeviceMesh('cuda', shape: {self.shape}, data: {self.mesh.tolist()})"

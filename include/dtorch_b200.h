@@ -55,11 +55,6 @@ typedef enum dt_redop {
  *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:123-130);
  *                     bit-identical to it. For fp32 both modes are the same left fold.
  *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size.
- *                     DT_ALGO_TWOSHOT (and reduce-scatter with it) pulls the peers' inputs in the reduce phase.
- *   DT_ALGO_PUSH      reduce phase by pushes instead: every rank stores the chunks the others own into their
- *                     staging (DTORCH_B200_STAGING_MB per rank, default 128, in the communicator's slab) and each
- *                     owner folds locally in rank order -- the same sum bit for bit. Default for all-reduce and
- *                     reduce-scatter from 1 MiB of chunk per rank when buffers and chunks are 16-byte multiples.
  *   DT_ALGO_NVLS      reduce inside the NVSwitch (NVLink SHARP): needs input and output in the communicator's
  *                     NVLS buffer (dt_comm_nvls_*); fp32 accumulation in the switch's order, not rank order.
  *                     Picked by default for such buffers at >= 6 ranks from 8 MiB (where it measured faster
@@ -70,7 +65,6 @@ typedef enum dt_redop {
 #define DT_ALGO_ONESHOT 0x10
 #define DT_ALGO_TWOSHOT 0x20
 #define DT_ALGO_NVLS 0x40
-#define DT_ALGO_PUSH 0x80
 
 typedef struct dt_comm dt_comm;
 

@@ -713,51 +713,3 @@ def test_all_to_all_multi_one_launch(mode):
         assert launched == (1 if mode == "same" else n), launched
     finally:
         comm.destroy()
-
-
-@pytest.mark.parametrize("staging_mb", [1, 128])
-@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
-def test_push_reduce_matches_restatement(staging_mb, dt, monkeypatch):
-    """The push-based reduce phase (DT_ALGO_PUSH): every rank stores the chunks others own into their staging,
-    owners fold in rank order. With 1 MiB of staging the message runs in many rounds (double-buffered windows,
-    a partial last one); back-to-back calls and in-place all-reduce reuse the round counters. Bit-exact against
-    the fp32-accumulate restatement, like the pull kernel."""
-    n = min(ngpu(), 8)
-    if n < 2:
-        pytest.skip("needs >= 2 GPUs")
-    monkeypatch.setenv("DTORCH_B200_STAGING_MB", str(staging_mb))
-    devs = list(range(n))
-    code, td = DT_CODE[dt], TD[dt]
-    es = torch.tensor([], dtype=td).element_size()
-    window = (staging_mb << 20) // (2 * n * 16) * 16 // es  # elements per staging slot
-    chunk = window * 3 + 16 // es * 5  # three full windows and a partial one
-    count = chunk * n
-    comm = capi.Comm(devs)
-    try:
-        comm.set_timeout_ms(20000)
-        g = torch.Generator().manual_seed(staging_mb + code)
-        for it in range(3):
-            host = [torch.randn(count, generator=g).to(td) for _ in range(n)]
-            d_in = [h.to(f"cuda:{r}") for r, h in enumerate(host)]
-            ar = [torch.empty_like(t) for t in d_in]
-            rs = [torch.empty(chunk, dtype=td, device=f"cuda:{r}") for r in range(n)]
-            inplace = [t.clone() for t in d_in]
-
-            def fn(r):
-                with torch.cuda.device(r):
-                    s = torch.cuda.current_stream(r).cuda_stream
-                    comm.all_reduce(r, d_in[r].data_ptr(), ar[r].data_ptr(), count, code, capi.DT_ALGO_PUSH, s)
-                    comm.reduce_scatter(r, d_in[r].data_ptr(), rs[r].data_ptr(), chunk, code, capi.DT_ALGO_PUSH, s)
-                    comm.all_reduce(r, inplace[r].data_ptr(), inplace[r].data_ptr(), count, code, capi.DT_ALGO_PUSH, s)
-                    torch.cuda.current_stream(r).synchronize()
-
-            run_ranks(n, fn)
-            raw = [raw_from_torch(h) for h in host]
-            want = R.fold_sum(raw, code, storage_round=False)
-            for r in range(n):
-                assert np.array_equal(np_raw(ar[r]), want), (it, r)
-                assert np.array_equal(np_raw(inplace[r]), want), (it, r)
-                assert np.array_equal(np_raw(rs[r]), want[r * chunk:(r + 1) * chunk]), (it, r)
-        assert comm.error(0) == capi.DT_OK
-    finally:
-        comm.destroy()
