@@ -463,6 +463,8 @@ int64_t copy_want_blocks(int64_t max_row_bytes, int64_t rows, int nseg) {
     return std::max<int64_t>(1, (items * nseg + warps - 1) / warps);
 }
 
+constexpr int64_t kShortRowSlots = 4 * 32;  // accesses per short-row item: 4 per lane (copy_rows_v)
+
 template <int VW>
 void set_geom(Seg& s) {
     s.vw = VW;
@@ -486,6 +488,16 @@ int launch_copy(CopyArgs<MAXSEG>& a, int dev, int num_sms, cudaStream_t stream, 
         const int64_t rows = s.cnt[0] * s.cnt[1] * s.cnt[2];
         s.spr = s.run > 0 ? (s.run + s.seg_bytes - 1) / s.seg_bytes : 0;
         s.items = rows * s.spr;
+        s.rpi = 0;
+        s.vpr = 0;
+        // short rows (at most a quarter of the lane slots each): several whole rows per item
+        const int64_t vpr = (s.run + s.vw - 1) / s.vw;
+        if (s.run > 0 && rows > 1 && vpr * 4 <= kShortRowSlots) {
+            s.vpr = static_cast<int32_t>(vpr);
+            s.rpi = static_cast<int32_t>(kShortRowSlots / vpr);
+            s.spr = 1;
+            s.items = (rows + s.rpi - 1) / s.rpi;
+        }
         a.max_items = std::max(a.max_items, s.items);
     }
     auto k = k_copy<MAXSEG, BAR>;

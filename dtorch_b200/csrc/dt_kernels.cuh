@@ -313,9 +313,11 @@ struct Seg {
     int64_t ss[3];     // source byte strides
     int64_t ds[3];     // destination byte strides
     int64_t spr;       // pieces per row
-    int64_t items;     // rows * spr
+    int64_t items;     // rows * spr, or ceil(rows / rpi) for short rows
     int32_t vw;        // access width in bytes: 16, 8, 4, 2 or 1
     int32_t seg_bytes; // bytes per piece (CopyGeom<vw>::kSegBytes)
+    int32_t rpi;       // > 1: short rows, rpi whole rows per item, one access per lane slot
+    int32_t vpr;       // short rows: accesses per row
 };
 
 template <int MAXSEG>
@@ -385,6 +387,41 @@ __device__ __noinline__ void copy_piece_narrow(const char* src, char* dst, int64
     }
 }
 
+constexpr int kShortRowSlotsDev = 4 * 32;  // accesses per short-row item (kShortRowSlots on the host)
+
+// Rows much shorter than an item (the all-to-all of a narrow dst-dim chunk, an all-gather of a thin shard): one
+// item holds `rpi` whole rows and each lane slot moves one access of one row, so every lane works instead of
+// one lane per row. Out of line, like the narrow path.
+template <typename V>
+__device__ __forceinline__ void copy_rows_v(const Seg& s, int64_t j, int lane) {
+    constexpr int64_t W = sizeof(V);
+    const int64_t rows = s.cnt[0] * s.cnt[1] * s.cnt[2];
+#pragma unroll 1
+    for (int f = lane; f < kShortRowSlotsDev; f += 32) {
+        const int r = f / s.vpr;
+        const int64_t row = j * s.rpi + r;
+        if (r >= s.rpi || row >= rows) break;
+        const int64_t off = static_cast<int64_t>(f - r * s.vpr) * W;
+        if (off >= s.run) continue;
+        const int64_t i2 = row % s.cnt[2];
+        const int64_t r01 = row / s.cnt[2];
+        const int64_t i1 = r01 % s.cnt[1];
+        const int64_t i0 = r01 / s.cnt[1];
+        *reinterpret_cast<V*>(s.dst + i0 * s.ds[0] + i1 * s.ds[1] + i2 * s.ds[2] + off) =
+            *reinterpret_cast<const V*>(s.src + i0 * s.ss[0] + i1 * s.ss[1] + i2 * s.ss[2] + off);
+    }
+}
+
+__device__ __noinline__ void copy_short_rows(const Seg& s, int64_t j, int lane) {
+    switch (s.vw) {
+        case 16: copy_rows_v<uint4>(s, j, lane); break;
+        case 8: copy_rows_v<uint2>(s, j, lane); break;
+        case 4: copy_rows_v<uint32_t>(s, j, lane); break;
+        case 2: copy_rows_v<uint16_t>(s, j, lane); break;
+        default: copy_rows_v<uint8_t>(s, j, lane); break;
+    }
+}
+
 template <int MAXSEG, bool BARRIER>
 __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyArgs<MAXSEG> a) {
     uint32_t e = 0;
@@ -401,6 +438,10 @@ __global__ void __launch_bounds__(kThreads) k_copy(const __grid_constant__ CopyA
         const int64_t j = t / a.nseg;
         const Seg& s = a.seg[d];
         if (j >= s.items) continue;
+        if (s.rpi > 1) {
+            copy_short_rows(s, j, lane);
+            continue;
+        }
         int64_t row = j, sg = 0;
         if (s.spr != 1) {
             row = j / s.spr;

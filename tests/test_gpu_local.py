@@ -172,3 +172,35 @@ def test_local_all_reduce_from_host_buffers_in_place(chunk):
     s.synchronize()
     assert np.array_equal(raw_from_torch(host[1]), want)
     assert np.array_equal(np_raw(dev[2]), want)
+
+
+@pytest.mark.parametrize("dt,shape,sd,dd", [
+    ("bfloat16", (4096, 64), 0, 1),        # 16-byte runs per (row, destination)
+    ("float32", (2048, 24), 0, 1),         # 12-byte runs: 4-byte accesses, uneven split of 24 over 8 ranks
+    ("float16", (3, 1000, 10, 2), 1, 2),   # 4-byte runs under two outer dims
+])
+def test_local_all_to_all_short_rows(dt, shape, sd, dd):
+    """All-to-alls whose rows are far shorter than a copy item: several whole rows per warp item, one access per
+    lane, bit-exact against the restatement."""
+    n = 8
+    g = torch.Generator().manual_seed(sum(shape))
+    lens = shard_sizes(shape[sd], n)
+    host = []
+    for l in lens:
+        s = list(shape)
+        s[sd] = l
+        host.append(torch.randn(*s, generator=g).to(TD[dt]))
+    split = shard_sizes(shape[dd], n)
+    d_in = [h.to("cuda:0") for h in host]
+    d_out = []
+    for k in range(n):
+        s = list(shape)
+        s[dd] = split[k]
+        d_out.append(torch.empty(*s, dtype=TD[dt], device="cuda:0"))
+    in_shape = list(host[0].shape)
+    capi.local_all_to_all([t.data_ptr() for t in d_in], [t.data_ptr() for t in d_out], in_shape, sd, dd, lens,
+                          host[0].element_size())
+    torch.cuda.synchronize()
+    want = R.all_to_all([raw_from_torch(h) for h in host], sd, dd)
+    for k in range(n):
+        assert np.array_equal(np_raw(d_out[k]).reshape(want[k].shape), want[k]), k
