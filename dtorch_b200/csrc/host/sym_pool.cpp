@@ -155,21 +155,37 @@ torch::Tensor SymmetricPool::Empty(int rank, at::IntArrayRef shape, const at::Te
     const size_t bytes = std::max<size_t>(kAlign, (bytes_all_ranks + kAlign - 1) / kAlign * kAlign);
     std::shared_ptr<Block> b;
     {
-        std::lock_guard<std::mutex> lock(mMutex);
+        std::unique_lock<std::mutex> lock(mMutex);
         const uint64_t k = mSeq[static_cast<size_t>(rank)]++;
         auto it = mPending.find(k);
         if (it == mPending.end()) {
+            // first rank at allocation k: pick the block for every rank
             b = std::make_shared<Block>();
             b->bytes = bytes;
+            b->resolving = true;
+            mPending[k] = b;
             Reclaim(false);
-            if (!Fit(bytes, &b->off)) {
-                Reclaim(true);
-                if (!Fit(bytes, &b->off)) b->failed = true;
+            while (!Fit(bytes, &b->off)) {
+                if (mReleased.empty()) {
+                    b->failed = true;
+                    break;
+                }
+                // wait for the oldest released block's GPU work WITHOUT holding the lock: that work may depend on
+                // kernels other rank threads still have to launch, and they may need the lock to get there
+                std::vector<std::pair<int, cudaEvent_t>> evs = mReleased.front()->freed;
+                lock.unlock();
+                for (auto& re : evs)
+                    if (re.second != nullptr) cudaEventSynchronize(re.second);
+                cudaGetLastError();
+                lock.lock();
+                Reclaim(false);
             }
             if (!b->failed) mInUse += bytes;
-            mPending[k] = b;
+            b->resolving = false;
+            mResolved.notify_all();
         } else {
             b = it->second;
+            mResolved.wait(lock, [&] { return !b->resolving; });
             if (b->bytes != bytes)
                 throw std::logic_error("SymmetricPool: ranks asked for different sizes at allocation " +
                                        std::to_string(k) + " (collectives issued out of order?)");

@@ -13,13 +13,17 @@
 //
 // Lifetime: a block returns to the free list once every rank's tensor is gone and the GPU has passed the
 // points at which they were freed (events recorded on the freeing thread's current stream and on the rank's
-// kernel stream, polled on the host), so memory is never reused while a kernel may still touch it. A tensor
+// kernel stream, polled on the host), so memory is never reused while a kernel may still touch it. When no range
+// fits, the first rank waits for the oldest released block's events with the pool unlocked (that GPU work may
+// depend on kernels other rank threads still have to launch); if nothing is left to wait for, every rank gets
+// an ordinary allocation instead. A tensor
 // used on any other stream must be synchronized by its user before it is freed (the rule of torch's caching
 // allocator without recordStream).
 #pragma once
 
 #include <cuda_runtime.h>
 
+#include <condition_variable>
 #include <cstdint>
 #include <deque>
 #include <map>
@@ -61,7 +65,8 @@ private:
         size_t bytes = 0;
         int taken = 0;   // ranks that received their tensor
         int live = 0;    // ranks whose tensor is still alive
-        bool failed = false;  // the pool had no room: every rank gets an undefined tensor
+        bool failed = false;     // the pool had no room: every rank gets an undefined tensor
+        bool resolving = false;  // the first rank is still finding room for it (others wait on mResolved)
         std::vector<std::pair<int, cudaEvent_t>> freed;  // (rank, event) recorded when a rank's tensor died
     };
 
@@ -76,6 +81,7 @@ private:
     size_t mBytes;
     bool mNvls;
     std::mutex mMutex;
+    std::condition_variable mResolved;
     std::map<size_t, size_t> mFree;                      // offset -> length, coalesced
     std::vector<uint64_t> mSeq;                          // per rank: allocations made so far
     std::map<uint64_t, std::shared_ptr<Block>> mPending;  // allocation index -> block not yet taken by all ranks
