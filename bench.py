@@ -907,15 +907,45 @@ def run_ours_multi(args, rank, world, local_rank):
     pv = torch.tensor([0.0 if par.ok else 1.0, 0.0 if par.bit_exact else 1.0, par.max_abs,
                        0.0 if (p2p_par is None or p2p_par.ok) else 1.0], device=dev, dtype=torch.float64)
     dist.all_reduce(pv, op=dist.ReduceOp.MAX)
-    del want
     # end to end: pinned host input -> heap, collective, heap output -> pinned host
     h_in = x.cpu().pin_memory()
     h_out = torch.empty(out_numel, dtype=dtype).pin_memory()
+    e2e_path = "C ABI (dt_* on a multi-process dt_comm) with pinned host buffers, copy - collective - copy"
 
     def e2e_step():
         x.copy_(h_in, non_blocking=True)
         step()
         h_out.copy_(y, non_blocking=True)
+
+    if op == "all_reduce":
+        # the all-reduce chunk by chunk (every rank the same chunks), so the H2D of chunk i+1, the collective on
+        # chunk i and the D2H of chunk i-1 overlap -- what dt_local_all_reduce_host does inside the library at N = 1
+        per = 16 // es
+        step_elems = max(per, ((16 << 20) // es) // per * per)
+        chunks = [(lo, min(in_numel, lo + step_elems)) for lo in range(0, in_numel, step_elems)]
+        h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev_start, ev_end = torch.cuda.Event(), torch.cuda.Event()
+        ev_in, ev_red = torch.cuda.Event(), torch.cuda.Event()
+        e2e_path = ("C ABI dt_all_reduce per 16 MiB chunk on a multi-process dt_comm, pinned host buffers; H2D, "
+                    "collective and D2H of consecutive chunks overlapping")
+
+        def e2e_step():  # noqa: F811 (the chunked variant for the all-reduce)
+            ev_start.record(stream)
+            h2d_s.wait_event(ev_start)
+            d2h_s.wait_event(ev_start)
+            for lo, hi in chunks:
+                with torch.cuda.stream(h2d_s):
+                    x[lo:hi].copy_(h_in[lo:hi], non_blocking=True)
+                ev_in.record(h2d_s)
+                stream.wait_event(ev_in)
+                comm.all_reduce(rank, x.data_ptr() + lo * es, y.data_ptr() + lo * es, hi - lo, code, ar_flags,
+                                stream.cuda_stream)
+                ev_red.record(stream)
+                d2h_s.wait_event(ev_red)
+                with torch.cuda.stream(d2h_s):
+                    h_out[lo:hi].copy_(y[lo:hi], non_blocking=True)
+            ev_end.record(d2h_s)
+            stream.wait_event(ev_end)
 
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()
@@ -926,6 +956,13 @@ def run_ours_multi(args, rank, world, local_rank):
     t_max = torch.tensor([e2e_ms], device=dev)
     dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     e2e_ms = float(t_max.item())
+    # the host result of the last end-to-end step against the same expected output
+    e2e_par = Parity(dtype, tolerance=(ar_flags == capi.DT_ALGO_NVLS))
+    e2e_par.compare(raw_np(h_out), want)
+    ev2 = torch.tensor([0.0 if e2e_par.ok else 1.0], device=dev, dtype=torch.float64)
+    dist.all_reduce(ev2, op=dist.ReduceOp.MAX)
+    e2e_ok = ev2.item() == 0.0
+    del want
     # NCCL on the same message, for the algorithm table (not the product path)
     nccl_bus = None
     if op in ("all_reduce", "all_gather", "reduce_scatter"):
@@ -1000,11 +1037,12 @@ def run_ours_multi(args, rank, world, local_rank):
             "parity": {"checked": True, "ok": pv[0].item() == 0.0 and pv[3].item() == 0.0,
                        "bit_exact": pv[1].item() == 0.0, "max_abs_err": float(pv[2].item()), "ranks": n,
                        "rule": par.summary("")["rule"], "p2p_leg_ok": None if p2p_par is None else pv[3].item() == 0.0,
+                       "e2e_ok": e2e_ok,
                        "against": "C restatement of the reference's algorithm (oracle/dt_oracle.c), fp32 "
                                   "accumulation in rank order, on every rank's full output"},
             "e2e": {"value": round(e2e_bus * n, 3), "unit": "GB/s", "h2d_bytes_per_step": in_numel * es,
                     "d2h_bytes_per_step": out_numel * es, "ms_per_step": round(e2e_ms, 4),
-                    "path": "C ABI (dt_* on a multi-process dt_comm) with pinned host buffers"},
+                    "path": e2e_path},
             "gpu_launches": launches,
             "device_error": err,
             "clocks": clk.summary(),
@@ -1014,7 +1052,7 @@ def run_ours_multi(args, rank, world, local_rank):
     dist.barrier()
     dist.destroy_process_group()
     api_bad = rank == 0 and isinstance(api, dict) and "parity" in api and not api["parity"]["ok"]
-    if pv[0].item() != 0.0 or pv[3].item() != 0.0 or api_bad:
+    if pv[0].item() != 0.0 or pv[3].item() != 0.0 or not e2e_ok or api_bad:
         if rank == 0:
             print("parity check failed: the timed collective's output differs from the oracle", file=sys.stderr)
         sys.exit(3)
