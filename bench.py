@@ -1089,7 +1089,10 @@ def run_sweep_multi(args, rank, world, local_rank):
 
     comm = create_rank_comm(2 * max_bytes + (4 << 20), local_rank)
     base, _ = comm.heap(rank)
-    stream = torch.cuda.current_stream(dev)
+    # a side stream made current for the whole sweep: our calls, NCCL's and the CUDA-graph captures
+    # (which cannot run on the default stream) all order on it
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     ops = args.sweep_ops.split(",")
     nvls_base = 0
     if "all_reduce" in ops and args.algo != "p2p" and (n >= 4 or args.algo == "nvls"):  # sweep: compare at 4 too
@@ -1179,7 +1182,7 @@ def run_sweep_multi(args, rank, world, local_rank):
                         g = torch.cuda.CUDAGraph()
                         dist.barrier()
                         torch.cuda.synchronize()
-                        with torch.cuda.graph(g, stream=stream):
+                        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
                             for _ in range(iters):
                                 fn()
                         torch.cuda.synchronize()
