@@ -26,9 +26,11 @@ DT_FLOAT32, DT_BFLOAT16, DT_FLOAT16 = 0, 1, 2
 DT_SUM = 0
 DT_ACCUM_FP32 = 0x0
 DT_ACCUM_STORAGE = 0x1
+DT_RANK_ORDER = 0x2
 DT_ALGO_ONESHOT = 0x10
 DT_ALGO_TWOSHOT = 0x20
 DT_ALGO_NVLS = 0x40
+DT_ALGO_NCCL = 0x80
 
 MAX_RANKS = 8
 

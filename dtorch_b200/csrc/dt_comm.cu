@@ -22,8 +22,11 @@
 #include <memory>
 #include <vector>
 
+#include <dlfcn.h>
+
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <nccl.h>  // types only: the functions are looked up at run time (nccl_api)
 
 #include "../../include/dtorch_b200.h"
 #include "dt_kernels.cuh"
@@ -145,6 +148,13 @@ struct dt_comm {
     bool nvls_have_mc = false;
     size_t nvls_size = 0;
     CUdeviceptr nvls_mc_va = 0;  // single process: one multicast mapping shared by every rank
+    // NCCL clique over the same devices (single-process peer mode), made by the first call routed to NCCL
+    std::mutex nccl_mu;
+    std::atomic<int> nccl_state{0};  // 0: not tried, 1: ready, -1: unavailable (nccl_err says why)
+    std::string nccl_err;
+    ncclComm_t nccl[kMaxRanks] = {};
+    bool nccl_route = true;   // DTORCH_B200_NCCL != 0: DT_ALGO_AUTO may route to NCCL where it measured faster
+    bool rank_order = false;  // DTORCH_B200_RANK_ORDER=1: every call behaves as if DT_RANK_ORDER were set
 };
 
 namespace {
@@ -156,6 +166,43 @@ int64_t env_timeout_ms() {
         if (v > 0) return static_cast<int64_t>(v) * 1000;
     }
     return 600 * 1000;  // the reference's default (global_option.cc:20)
+}
+
+bool env_flag(const char* name, bool dflt) {
+    const char* s = std::getenv(name);
+    if (s == nullptr || *s == '\0') return dflt;
+    return !(s[0] == '0' && s[1] == '\0');
+}
+
+// ---- NCCL, for the messages where it measured faster -------------------------------------------------------
+// Looked up at run time -- the copy the process already loaded (torch's), else libnccl.so.2 from the library
+// path -- so the library has no link-time dependency on it and a process without NCCL never routes there.
+struct NcclApi {
+    bool ok = false;
+    int version = 0;
+    ncclResult_t (*init_all)(ncclComm_t*, int, const int*) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl_api() {
+    static const NcclApi api = [] {
+        NcclApi a;
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (h == nullptr) return a;
+        a.init_all = reinterpret_cast<decltype(a.init_all)>(dlsym(h, "ncclCommInitAll"));
+        a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
+        a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+        auto get_version = reinterpret_cast<ncclResult_t (*)(int*)>(dlsym(h, "ncclGetVersion"));
+        if (get_version != nullptr) get_version(&a.version);
+        a.ok = a.init_all && a.all_reduce && a.destroy && a.error_string;
+        return a;
+    }();
+    return api;
 }
 
 bool check_rank(const dt_comm* c, int rank) {
@@ -931,6 +978,50 @@ int current_device_sms(int* dev, int* sms) {
     return DT_OK;
 }
 
+// The communicator's NCCL clique, made once by whichever rank thread gets here first (ncclCommInitAll over the
+// communicator's devices, in rank order) while the other rank threads wait; every rank thread then sees the
+// same outcome, so all ranks route a call the same way. Single-process peer mode only: a multi-process
+// communicator has no host channel of its own for NCCL's unique id. Returns true when the clique is usable.
+bool nccl_ready(dt_comm* c) {
+    if (c->multiprocess || c->same_device || c->n < 2) return false;
+    const int state = c->nccl_state.load(std::memory_order_acquire);
+    if (state != 0) return state > 0;
+    std::lock_guard<std::mutex> g(c->nccl_mu);
+    if (c->nccl_state.load(std::memory_order_relaxed) == 0) {
+        const NcclApi& api = nccl_api();
+        int st = -1;
+        if (!api.ok) {
+            c->nccl_err = "libnccl.so.2 could not be loaded";
+        } else {
+            int devs[kMaxRanks];
+            for (int r = 0; r < c->n; ++r) devs[r] = c->r[r].dev;
+            DeviceGuard device_guard;
+            const ncclResult_t e = api.init_all(c->nccl, c->n, devs);
+            if (e == ncclSuccess) {
+                st = 1;
+            } else {
+                c->nccl_err = std::string("ncclCommInitAll: ") + api.error_string(e);
+                for (int r = 0; r < c->n; ++r) c->nccl[r] = nullptr;
+            }
+        }
+        c->nccl_state.store(st, std::memory_order_release);
+    }
+    return c->nccl_state.load(std::memory_order_relaxed) > 0;
+}
+
+int nccl_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count, int dtype, cudaStream_t stream) {
+    if (!nccl_ready(c)) {
+        if (c->multiprocess || c->same_device)
+            return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NCCL: only for a single-process communicator in peer mode");
+        return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NCCL: " + c->nccl_err);
+    }
+    const ncclDataType_t t = dtype == DT_FLOAT32 ? ncclFloat32 : dtype == DT_BFLOAT16 ? ncclBfloat16 : ncclFloat16;
+    const NcclApi& api = nccl_api();
+    const ncclResult_t e = api.all_reduce(in, out, count, t, ncclSum, c->nccl[rank], stream);
+    if (e != ncclSuccess) return fail(DT_ERR_CUDA, std::string("ncclAllReduce: ") + api.error_string(e));
+    return DT_OK;
+}
+
 }  // namespace
 
 // =============================================================================================================
@@ -983,6 +1074,8 @@ int dt_comm_create(int nranks, const int* cuda_devices, size_t heap_bytes, dt_co
     c->same_device = same && nranks > 1;
     c->heap_bytes = heap_bytes;
     c->timeout_ms = env_timeout_ms();
+    c->nccl_route = env_flag("DTORCH_B200_NCCL", true);
+    c->rank_order = env_flag("DTORCH_B200_RANK_ORDER", false);
     c->arrived[0] = 0;
     c->arrived[1] = 0;
     int st = DT_OK;
@@ -1039,6 +1132,7 @@ int dt_comm_create_rank(int nranks, int rank, int cuda_device, size_t heap_bytes
     c->local_rank = rank;
     c->heap_bytes = heap_bytes;
     c->timeout_ms = env_timeout_ms();
+    c->rank_order = env_flag("DTORCH_B200_RANK_ORDER", false);
     int st = alloc_rank(c, rank, cuda_device, heap_bytes);
     if (st != DT_OK) {
         std::string msg = g_err;
@@ -1101,6 +1195,11 @@ int dt_comm_destroy(dt_comm* c) {
         cudaSetDevice(c->r[i].dev);
         cudaDeviceSynchronize();
     }
+    if (c->nccl_state.load() > 0) {
+        // one thread destroys the whole clique, as it was made (NCCL frees the shared parts with the last one)
+        for (int i = 0; i < c->n; ++i)
+            if (c->nccl[i] != nullptr) nccl_api().destroy(c->nccl[i]);
+    }
     nvls_release(c);
     for (int i = 0; i < kMaxRanks; ++i) {
         RankState& s = c->r[i];
@@ -1160,6 +1259,16 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
     cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
     RankState& s = c->r[rank];
     const bool storage = (flags & DT_ACCUM_STORAGE) != 0;
+    const bool rank_order = (flags & DT_RANK_ORDER) != 0 || c->rank_order;
+    constexpr int kAlgoBits = DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT | DT_ALGO_NVLS | DT_ALGO_NCCL;
+    if ((flags & DT_ALGO_NCCL) != 0) {
+        if ((flags & kAlgoBits) != DT_ALGO_NCCL) return fail(DT_ERR_INVALID, "DT_ALGO_NCCL with another DT_ALGO_* flag");
+        if (storage || rank_order)
+            return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NCCL sums in NCCL's order and precision; DT_ACCUM_STORAGE and "
+                                            "DT_RANK_ORDER are not available with it");
+        if (c->same_device || c->multiprocess)
+            return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NCCL: only for a single-process communicator in peer mode");
+    }
     if (c->same_device) {
         return same_device_call(c, rank, in, out, stream, [&](const Slot* all, cudaStream_t st0) -> int {
             const char* ins[kMaxRanks];
@@ -1180,6 +1289,7 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
         if (count > 0 && in != out) DT_CUDA(cudaMemcpyAsync(out, in, count * es, cudaMemcpyDeviceToDevice, stream));
         return DT_OK;
     }
+    if ((flags & DT_ALGO_NCCL) != 0) return nccl_all_reduce(c, rank, in, out, count, dtype, stream);
     // NVLS: input and output inside the communicator's NVLS buffer (same offsets on every rank)
     {
         int64_t nv_in = -1, nv_out = -1;
@@ -1205,8 +1315,8 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
         // at 4 ranks the two are level within 2 % either way from 16 MiB to 1 GiB (128 MiB: 645 vs 653), so
         // the rank-order fold stays; at 2 ranks NVLS is behind (it moves (1+1/n)S per GPU against 2(n-1)/n S)
         const size_t nvls_min = static_cast<size_t>(8) << 20;
-        const bool auto_nvls = (flags & (DT_ALGO_ONESHOT | DT_ALGO_TWOSHOT | DT_ALGO_NVLS)) == 0 && nvls_ok && !storage &&
-                               c->n >= 6 && bytes >= nvls_min;
+        const bool auto_nvls = (flags & kAlgoBits) == 0 && nvls_ok && !storage && !rank_order && c->n >= 6 &&
+                               bytes >= nvls_min;
         if (want_nvls || auto_nvls) {
             NvlsArgs na{};
             na.sig = make_sig(c, rank);
@@ -1224,6 +1334,14 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
             }
         }
     }
+    // NCCL where it measured faster: at 8 GPUs on ordinary buffers from 256 MiB (per-rank bus 657 vs 646 GB/s
+    // at 256 MiB, 704 vs 655 at 512 MiB, 726 vs 662 at 1 GiB); at 2 and 4 ranks the rank-order two-shot kernel is
+    // ahead at every size from 2 MiB up, and below 256 MiB at 8 ranks too. Every input of the decision is the
+    // same on every rank (flags, count, the communicator's shared clique state).
+    const size_t nccl_min = static_cast<size_t>(256) << 20;
+    if ((flags & kAlgoBits) == 0 && !storage && !rank_order && c->nccl_route && c->n >= 8 &&
+        count * es >= nccl_min && nccl_ready(c))
+        return nccl_all_reduce(c, rank, in, out, count, dtype, stream);
     ReduceArgs a{};
     const char* ins[kMaxRanks];
     char* outs[kMaxRanks];

@@ -54,17 +54,29 @@ typedef enum dt_redop {
  *   DT_ACCUM_STORAGE  round to the storage type after every add, which is what the reference's CPU fold
  *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:123-130);
  *                     bit-identical to it. For fp32 both modes are the same left fold.
+ *   DT_RANK_ORDER     keep the rank-order fold whatever the size: DT_ALGO_AUTO then never picks NVLS or NCCL
+ *                     (also set for every call by the environment variable DTORCH_B200_RANK_ORDER=1).
  *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size.
  *   DT_ALGO_NVLS      reduce inside the NVSwitch (NVLink SHARP): needs input and output in the communicator's
  *                     NVLS buffer (dt_comm_nvls_*); fp32 accumulation in the switch's order, not rank order.
  *                     Picked by default for such buffers at >= 6 ranks from 8 MiB (where it measured faster
- *                     than the rank-order kernels; at 4 ranks they are level, so the rank-order fold stays). */
+ *                     than the rank-order kernels; at 4 ranks they are level, so the rank-order fold stays).
+ *   DT_ALGO_NCCL      ncclAllReduce on a clique of NCCL communicators over the same devices (the reference's
+ *                     own GPU backend, thread_group.cc:75-88), made by the first such call (ncclCommInitAll;
+ *                     that call must not be captured in a CUDA graph). NCCL's summation order, and for
+ *                     bf16/fp16 its precision (partial sums in the storage type); identical on every rank.
+ *                     Single-process peer mode only; libnccl.so.2 is looked up at run time (the copy the
+ *                     process already loaded first). Picked by default for ordinary buffers at 8 ranks from
+ *                     256 MiB, where it measured faster than the two-shot kernel (unless DT_RANK_ORDER,
+ *                     DT_ACCUM_STORAGE or DTORCH_B200_NCCL=0). */
 #define DT_ACCUM_FP32 0x0
 #define DT_ACCUM_STORAGE 0x1
+#define DT_RANK_ORDER 0x2
 #define DT_ALGO_AUTO 0x00
 #define DT_ALGO_ONESHOT 0x10
 #define DT_ALGO_TWOSHOT 0x20
 #define DT_ALGO_NVLS 0x40
+#define DT_ALGO_NCCL 0x80
 
 typedef struct dt_comm dt_comm;
 
@@ -131,7 +143,8 @@ int dt_comm_clear_error(dt_comm* comm, int rank);
 
 /* Partial -> Replicate. out[i] = sum over ranks r = 0..n-1 (in that order) of in_r[i], `count` elements.
  * Replaces ThreadGroup::AllReduce (thread_group.cc:127-141); `in` is not modified (the reference clones it
- * first, :136). in == out is allowed. */
+ * first, :136). in == out is allowed. The rank order holds for every call with DT_RANK_ORDER or
+ * DT_ACCUM_STORAGE; without them DT_ALGO_AUTO may pick NVLS or NCCL where those measured faster (flags). */
 int dt_all_reduce(dt_comm* comm, int rank, const void* in, void* out, size_t count, int dtype, int op, int flags,
                   void* stream);
 
