@@ -89,3 +89,17 @@ def test_header_is_plain_c_and_links(tmp_path):
                     f"-L{libdir}", "-ldtorch_b200", f"-Wl,-rpath,{libdir}"], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
     assert out.strip() == "1 timeout waiting for a peer"
+
+
+def test_flag_constants_match_header():
+    text = open(HEADER).read()
+    defines = dict(re.findall(r"^#define\s+(DT_[A-Z0-9_]+)\s+(0x[0-9a-fA-F]+|\d+)\s*$", text, flags=re.M))
+    flags = {k: int(v, 0) for k, v in defines.items() if k.startswith(("DT_ALGO_", "DT_ACCUM_", "DT_RANK_"))}
+    assert {"DT_ALGO_NCCL", "DT_RANK_ORDER", "DT_ALGO_NVLS", "DT_ACCUM_STORAGE"} <= set(flags)
+    for name, value in flags.items():
+        if name == "DT_ALGO_AUTO":
+            continue
+        assert getattr(capi, name) == value, name
+    # the reduction flags are distinct bits
+    bits = [v for k, v in flags.items() if v]
+    assert len(bits) == len(set(bits)) and all(v & (v - 1) == 0 for v in bits)
