@@ -277,9 +277,12 @@ class LocalWorkload:
             self.hbm_bytes = 2 * full.numel() * self.es
         self.in_ptrs = [t.data_ptr() for t in self.ins]
         self.out_ptrs = [t.data_ptr() for t in self.outs]
-        # pinned host copies for the end-to-end leg
-        self.h_ins = [t.cpu().pin_memory() for t in self.ins]
-        self.h_outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in self.outs]
+        # pinned host copies for the end-to-end leg, on the GPU's own NUMA node
+        from dtorch_b200.multiprocess import near_device
+
+        with near_device(torch.device(dev).index or 0):
+            self.h_ins = [t.cpu().pin_memory() for t in self.ins]
+            self.h_outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in self.outs]
         self.h2d = sum(t.numel() * self.es for t in self.ins)
         self.d2h = sum(t.numel() * self.es for t in self.outs)
 
@@ -908,8 +911,13 @@ def run_ours_multi(args, rank, world, local_rank):
                        0.0 if (p2p_par is None or p2p_par.ok) else 1.0], device=dev, dtype=torch.float64)
     dist.all_reduce(pv, op=dist.ReduceOp.MAX)
     # end to end: pinned host input -> heap, collective, heap output -> pinned host
-    h_in = x.cpu().pin_memory()
-    h_out = torch.empty(out_numel, dtype=dtype).pin_memory()
+    # pinned host buffers on this GPU's NUMA node: with every GPU of the box copying at once, buffers on the
+    # other socket would send their DMA over the socket interconnect
+    from dtorch_b200.multiprocess import near_device
+
+    with near_device(local_rank) as numa_cpus:
+        h_in = x.cpu().pin_memory()
+        h_out = torch.empty(out_numel, dtype=dtype).pin_memory()
     e2e_path = "C ABI (dt_* on a multi-process dt_comm) with pinned host buffers, copy - collective - copy"
 
     def e2e_step():
@@ -1042,7 +1050,7 @@ def run_ours_multi(args, rank, world, local_rank):
                                   "accumulation in rank order, on every rank's full output"},
             "e2e": {"value": round(e2e_bus * n, 3), "unit": "GB/s", "h2d_bytes_per_step": in_numel * es,
                     "d2h_bytes_per_step": out_numel * es, "ms_per_step": round(e2e_ms, 4),
-                    "path": e2e_path},
+                    "path": e2e_path, "host_buffers_numa_local": numa_cpus is not None},
             "gpu_launches": launches,
             "device_error": err,
             "clocks": clk.summary(),

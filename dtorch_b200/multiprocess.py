@@ -8,6 +8,7 @@ symmetric heap (or its NVLS buffer).
 
 from __future__ import annotations
 
+import contextlib
 import os
 import socket
 import tempfile
@@ -90,3 +91,45 @@ def device_view(ptr: int, numel: int, dtype, device) -> torch.Tensor:
     ts = {torch.float32: "<f4", torch.bfloat16: "<i2", torch.float16: "<i2", torch.uint8: "|u1"}[dtype]
     t = torch.as_tensor(_CAI(ptr, numel, ts), device=device)
     return t.view(dtype) if dtype in (torch.bfloat16, torch.float16) else t
+
+
+def parse_cpulist(text: str) -> set:
+    """CPUs of a Linux cpulist ("0-55,112-167")."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def device_local_cpus(device: int) -> set:
+    """CPUs on the NUMA node the GPU's PCIe link attaches to (sysfs ``local_cpulist``); empty if unknown."""
+    p = torch.cuda.get_device_properties(device)
+    path = f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/local_cpulist"
+    try:
+        with open(path) as f:
+            return parse_cpulist(f.read())
+    except OSError:
+        return set()
+
+
+@contextlib.contextmanager
+def near_device(device: int, cpus=None):
+    """Run the block on the calling thread with its CPUs limited to those local to `device`, so host memory
+    allocated in the block -- pinned staging buffers above all -- lands on the GPU's own NUMA node (the kernel's
+    default local placement) and their DMA does not cross the socket interconnect when every GPU of the box
+    copies at once. The thread's previous CPU set is restored afterwards; where the local CPUs are unknown or
+    not allowed to this process, the block runs unchanged. Yields the CPU set used (None when unchanged)."""
+    local = set(cpus) if cpus is not None else device_local_cpus(device)
+    old = os.sched_getaffinity(0)
+    use = local & old
+    if not use or use == old:
+        yield None
+        return
+    os.sched_setaffinity(0, use)
+    try:
+        yield use
+    finally:
+        os.sched_setaffinity(0, old)
