@@ -329,6 +329,33 @@ def time_steps(fn, steps, stream):
     return start.elapsed_time(end) / steps  # ms per step
 
 
+def l2_plan(in_bytes, device):
+    """How the timed steps keep L2 from serving the inputs: (flush, l2 bytes, description). Inputs larger than
+    L2 are not flushed; smaller ones get an L2 flush between timed steps (time_steps_flushed)."""
+    l2 = int(torch.cuda.get_device_properties(device).L2_cache_size)
+    mib = lambda b: f"{b / 2**20:.0f} MiB"  # noqa: E731
+    if in_bytes > l2:
+        return False, l2, f"inputs on this GPU ({mib(in_bytes)}) larger than L2 ({mib(l2)}); no flush"
+    return True, l2, (f"inputs on this GPU ({mib(in_bytes)}) fit in L2 ({mib(l2)}): L2 flushed between timed "
+                      f"steps (a {mib(2 * l2)} write outside each step's events)")
+
+
+def time_steps_flushed(fn, steps, stream, l2_bytes):
+    """ms per step with L2 flushed before every step: a write of twice L2 on `stream`, then the step between
+    its own pair of events; the steps' event times are summed."""
+    scratch = torch.empty(2 * l2_bytes // 4, dtype=torch.float32, device=stream.device)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i, (a, b) in enumerate(pairs):
+            scratch.fill_(float(i))
+            a.record(stream)
+            fn()
+            b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in pairs) / steps
+
+
 # ---------------------------------------------------------------------------------------------------------
 # CPU baseline: the reference's own thread-group code (oracle/_ref) on this host's cores
 # ---------------------------------------------------------------------------------------------------------
@@ -529,10 +556,12 @@ def run_ours_single(args):
         for _ in range(args.warmup):
             w.step()
     torch.cuda.synchronize()
+    flush, l2_bytes, l2_note = l2_plan(sum(t.numel() for t in w.ins) * w.es, 0)
     l0 = capi.launch_count()
     with ClockSampler(0) as clk:
         with torch.cuda.stream(stream):
-            ms = time_steps(w.step, args.steps, stream)
+            ms = (time_steps_flushed(w.step, args.steps, stream, l2_bytes) if flush
+                  else time_steps(w.step, args.steps, stream))
     launches = capi.launch_count() - l0
     # parity of what the timed steps wrote, against the restatement (outside the timed region)
     par = Parity(cfg["dtype"], tolerance=False)
@@ -578,7 +607,7 @@ def run_ours_single(args):
         "config": {"workload": cfg["name"] + f", same-device group of {n} ranks on 1 GPU (reference same-device "
                    "mode), one kernel per step", "op": op, "group_ranks": n, "msg_bytes_per_rank": w.msg_bytes,
                    "accumulate": "fp32, rank order" if op in ("all_reduce", "reduce_scatter") else "copy",
-                   "l2": "inputs larger than L2 (126 MB); no flush", "parallelism": "same-device"},
+                   "l2": l2_note, "parallelism": "same-device"},
         "bus_gbs_per_rank": round(bus, 2),
         "pct_nvlink_peak": None,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -865,6 +894,7 @@ def run_ours_multi(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    flush, l2_bytes, l2_note = l2_plan(in_numel * es, dev)
     nvl = NvLinkCounter(local_rank)
     l0 = capi.launch_count()
     with ClockSampler(local_rank) as clk:
@@ -872,7 +902,8 @@ def run_ours_multi(args, rank, world, local_rank):
         dist.barrier()
         torch.cuda.synchronize()
         c0 = nvl.read()
-        ms = time_steps(step, args.steps, stream)
+        ms = (time_steps_flushed(step, args.steps, stream, l2_bytes) if flush
+              else time_steps(step, args.steps, stream))
     launches = capi.launch_count() - l0
     time.sleep(0.05)
     c1 = nvl.read()
@@ -1025,7 +1056,7 @@ def run_ours_multi(args, rank, world, local_rank):
             "data": "synthetic (seeded, BASELINE.json distribution)",
             "config": {"workload": cfg["name"] + f" on {n} GPUs, one rank per GPU, P2P kernels over NVLink",
                        "op": op, "group_ranks": n, "msg_bytes_per_rank": msg,
-                       "l2": "per-rank buffers larger than L2; no flush", "parallelism": f"group{n}"},
+                       "l2": l2_note, "parallelism": f"group{n}"},
             "bus_gbs_per_rank": round(bus, 2),
             "pct_nvlink_peak": round(bus / NVLINK_NOMINAL_GBS, 4),
             "nccl_bus_gbs_per_rank": None if nccl_bus is None else round(nccl_bus, 2),
