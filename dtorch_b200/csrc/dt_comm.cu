@@ -1308,9 +1308,9 @@ int dt_all_reduce(dt_comm* c, int rank, const void* in, void* out, size_t count,
         if (want_nvls && !nvls_ok)
             return fail(DT_ERR_INVALID, "DT_ALGO_NVLS needs 16-byte aligned input and output inside the communicator's "
                                         "NVLS buffer and a size that is a multiple of 16 bytes");
-        if (want_nvls && storage)
-            return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NVLS reduces in the switch with fp32 accumulation; "
-                                            "DT_ACCUM_STORAGE is not available with it");
+        if (want_nvls && (storage || rank_order))
+            return fail(DT_ERR_UNSUPPORTED, "DT_ALGO_NVLS reduces in the switch's order with fp32 accumulation; "
+                                            "DT_ACCUM_STORAGE and DT_RANK_ORDER are not available with it");
         // measured: at 8 ranks NVLS is ahead of the two-shot kernel from 8-16 MiB (781 vs 633 GB/s at 128 MiB);
         // at 4 ranks the two are level within 2 % either way from 16 MiB to 1 GiB (128 MiB: 645 vs 653), so
         // the rank-order fold stays; at 2 ranks NVLS is behind (it moves (1+1/n)S per GPU against 2(n-1)/n S)

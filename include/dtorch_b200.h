@@ -54,8 +54,9 @@ typedef enum dt_redop {
  *   DT_ACCUM_STORAGE  round to the storage type after every add, which is what the reference's CPU fold
  *                     `result += x_r` does in bf16/fp16 (thread_group_same_device_backend.cc:123-130);
  *                     bit-identical to it. For fp32 both modes are the same left fold.
- *   DT_RANK_ORDER     keep the rank-order fold whatever the size: DT_ALGO_AUTO then never picks NVLS or NCCL
- *                     (also set for every call by the environment variable DTORCH_B200_RANK_ORDER=1).
+ *   DT_RANK_ORDER     keep the rank-order fold whatever the size: DT_ALGO_AUTO then never picks NVLS or NCCL,
+ *                     and forcing either is rejected (DT_ERR_UNSUPPORTED); the environment variable
+ *                     DTORCH_B200_RANK_ORDER=1 sets it for every call.
  *   DT_ALGO_ONESHOT / DT_ALGO_TWOSHOT force the all-reduce algorithm; default picks by message size.
  *   DT_ALGO_NVLS      reduce inside the NVSwitch (NVLink SHARP): needs input and output in the communicator's
  *                     NVLS buffer (dt_comm_nvls_*); fp32 accumulation in the switch's order, not rank order.

@@ -374,6 +374,10 @@ def test_nvls_all_reduce(dtype):
         with pytest.raises(capi.DtError):  # storage rounding is not available in the switch
             comm.all_reduce(0, xs[0].data_ptr(), ys[0].data_ptr(), count, code,
                             capi.DT_ALGO_NVLS | capi.DT_ACCUM_STORAGE, 0)
+        with pytest.raises(capi.DtError) as e:  # nor the rank-order fold
+            comm.all_reduce(0, xs[0].data_ptr(), ys[0].data_ptr(), count, code,
+                            capi.DT_ALGO_NVLS | capi.DT_RANK_ORDER, 0)
+        assert e.value.status == capi.DT_ERR_UNSUPPORTED
     finally:
         comm.destroy()
 
