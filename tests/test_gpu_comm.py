@@ -404,7 +404,7 @@ def test_nvls_picked_by_default_from_switch_over_size():
             xs[r].copy_(host[r].to(f"cuda:{r}"))
         torch.cuda.synchronize()
         outs = {}
-        for flags in (capi.DT_ALGO_NVLS, 0):
+        for flags in (capi.DT_ALGO_NVLS, 0, capi.DT_RANK_ORDER):
             def fn(r):
                 with torch.cuda.device(r):
                     s = torch.cuda.current_stream(r)
@@ -420,6 +420,7 @@ def test_nvls_picked_by_default_from_switch_over_size():
             else:  # the rank-order fold, bit for bit
                 assert np.array_equal(outs[0][r], want)
             assert_close(outs[0][r], want, "bfloat16")
+            assert np.array_equal(outs[capi.DT_RANK_ORDER][r], want)  # pinned to the fold at any group size
     finally:
         comm.destroy()
 
