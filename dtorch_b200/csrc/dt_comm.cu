@@ -1044,7 +1044,7 @@ const char* dt_status_string(int status) {
 
 const char* dt_last_error_message(void) { return g_err.c_str(); }
 
-int dt_version(void) { return (1 << 16) | 0; }
+int dt_version(void) { return (1 << 16) | 1; }
 
 uint64_t dt_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
