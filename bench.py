@@ -337,18 +337,21 @@ def l2_plan(in_bytes, device):
     if in_bytes > l2:
         return False, l2, f"inputs on this GPU ({mib(in_bytes)}) larger than L2 ({mib(l2)}); no flush"
     return True, l2, (f"inputs on this GPU ({mib(in_bytes)}) fit in L2 ({mib(l2)}): L2 flushed between timed "
-                      f"steps (a {mib(2 * l2)} write outside each step's events)")
+                      f"steps (a {mib(2 * l2)} write, then a read of it, outside each step's events)")
 
 
 def time_steps_flushed(fn, steps, stream, l2_bytes):
-    """ms per step with L2 flushed before every step: a write of twice L2 on `stream`, then the step between
-    its own pair of events; the steps' event times are summed."""
+    """ms per step with L2 flushed before every step: a write of twice L2 on `stream`, then a read of the same
+    buffer (so L2 is left holding clean lines and the step pays for no write-back of the flush), then the step
+    between its own pair of events; the steps' event times are summed."""
     scratch = torch.empty(2 * l2_bytes // 4, dtype=torch.float32, device=stream.device)
+    sink = torch.empty((), dtype=torch.float32, device=stream.device)
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         for i, (a, b) in enumerate(pairs):
             scratch.fill_(float(i))
+            torch.amax(scratch, dim=0, out=sink)
             a.record(stream)
             fn()
             b.record(stream)
