@@ -65,7 +65,8 @@ typedef enum dt_redop {
  *   DT_ALGO_NCCL      ncclAllReduce on a clique of NCCL communicators over the same devices (the reference's
  *                     own GPU backend, thread_group.cc:75-88), made by the first such call (ncclCommInitAll;
  *                     that call must not be captured in a CUDA graph). NCCL's summation order, and for
- *                     bf16/fp16 its precision (partial sums in the storage type); identical on every rank.
+ *                     bf16/fp16 its precision (partial sums in the storage type); identical on every rank;
+ *                     its waits are NCCL's, not bounded by the communicator's timeout.
  *                     Single-process peer mode only; libnccl.so.2 is looked up at run time (the copy the
  *                     process already loaded first). Picked by default for ordinary buffers at 8 ranks from
  *                     256 MiB, where it measured faster than the two-shot kernel (unless DT_RANK_ORDER,
