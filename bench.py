@@ -1264,6 +1264,78 @@ def run_sweep_multi(args, rank, world, local_rank):
     dist.destroy_process_group()
 
 
+def run_sweep_single_process(args):
+    """All-reduce sweep in the reference's process model: one process drives every visible GPU, one host thread
+    per rank, ordinary (torch-allocated) buffers. Per size: the default choice (NCCL at 8 ranks from 256 MiB,
+    the rank-order two-shot kernel otherwise), DT_RANK_ORDER (always the two-shot kernel) and DT_ALGO_NCCL,
+    timed with CUDA events on every rank's stream, max over ranks; how many of this library's kernels the
+    default choice launched (0 = NCCL ran it); and the default result checked against the rank-order one
+    with every rank's copy equal."""
+    import threading
+
+    from dtorch_b200 import capi
+
+    n = torch.cuda.device_count() if args.gpus <= 1 else args.gpus
+    comm = capi.Comm(list(range(n)))
+    variants = (("auto", 0), ("rank_order", capi.DT_RANK_ORDER), ("nccl", capi.DT_ALGO_NCCL))
+    try:
+        for dtype in (torch.bfloat16,):
+            es = torch.tensor([], dtype=dtype).element_size()
+            code = capi.dtype_code(dtype)
+            for S in sweep_sizes(args.sweep_lo, args.sweep_hi):
+                count = S // es
+                gens = [torch.Generator(device=f"cuda:{r}").manual_seed(r) for r in range(n)]
+                xs = [torch.randn(count, device=f"cuda:{r}", generator=gens[r]).to(dtype) for r in range(n)]
+                outs = {name: [torch.empty_like(x) for x in xs] for name, _ in variants}
+                row = {"sweep": "all_reduce_single_process", "n_gpus": n, "dtype": DT_NAME[dtype], "bytes": S}
+                for name, flags in variants:
+                    times, launched = [0.0] * n, {}
+                    bar = threading.Barrier(n)
+                    ys = outs[name]
+
+                    def fn(r):
+                        with torch.cuda.device(r):
+                            st = torch.cuda.current_stream(r)
+                            for _ in range(3):
+                                comm.all_reduce(r, xs[r].data_ptr(), ys[r].data_ptr(), count, code, flags, st.cuda_stream)
+                            st.synchronize()
+                            bar.wait(timeout=300)
+                            if r == 0:
+                                launched["a"] = capi.launch_count()
+                            bar.wait(timeout=300)
+                            e0 = torch.cuda.Event(enable_timing=True)
+                            e1 = torch.cuda.Event(enable_timing=True)
+                            e0.record(st)
+                            for _ in range(args.steps):
+                                comm.all_reduce(r, xs[r].data_ptr(), ys[r].data_ptr(), count, code, flags, st.cuda_stream)
+                            e1.record(st)
+                            e1.synchronize()
+                            times[r] = e0.elapsed_time(e1) / args.steps
+                            bar.wait(timeout=300)
+                            if r == 0:
+                                launched["b"] = capi.launch_count()
+
+                    ts = [threading.Thread(target=fn, args=(r,)) for r in range(n)]
+                    for t in ts:
+                        t.start()
+                    for t in ts:
+                        t.join()
+                    ms = max(times)
+                    row[f"{name}_ms"] = round(ms, 5)
+                    row[f"{name}_bus_gbs"] = round(S * bus_factor("all_reduce", n) / ms / 1e6, 2)
+                    row[f"{name}_our_launches_per_call"] = (launched["b"] - launched["a"]) / args.steps / n
+                ref = outs["rank_order"][0].float()
+                rms = float(ref.pow(2).mean().sqrt())
+                ok = all(torch.equal(outs["rank_order"][r].to("cuda:0"), outs["rank_order"][0]) and
+                         torch.equal(outs["auto"][r].to("cuda:0"), outs["auto"][0]) for r in range(n))
+                ok = ok and bool(torch.allclose(outs["auto"][0].float(), ref, rtol=2e-2, atol=2e-2 * rms))
+                row["auto_within_tolerance_of_rank_order"] = ok
+                print(json.dumps(row), flush=True)
+                del xs, outs
+    finally:
+        comm.destroy()
+
+
 def run_sweep_single(args):
     """1 GPU: the same-device kernels for a group of `emul_n` ranks against HBM."""
     from dtorch_b200 import capi
@@ -1342,6 +1414,8 @@ def main():
     p.add_argument("--sweep-ops", default="all_reduce,all_gather,reduce_scatter,all_to_all")
     p.add_argument("--sweep-no-nccl", action="store_true", help="sweep without the NCCL comparison")
     p.add_argument("--sweep-graph", action="store_true", help="sweep: also time our calls replayed from a CUDA graph")
+    p.add_argument("--sweep-single-process", action="store_true",
+                   help="all-reduce sweep with one process driving every GPU (default choice, DT_RANK_ORDER, NCCL)")
     p.add_argument("--sweep-flags", type=int, default=0, help="sweep: reduction flags of our all-reduce / reduce-scatter (e.g. 0x20 forces the two-shot kernel)")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -1351,7 +1425,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    if args.sweep:
+    if args.sweep_single_process:
+        run_sweep_single_process(args)
+    elif args.sweep:
         run_sweep_multi(args, rank, world, local_rank) if world > 1 else run_sweep_single(args)
     elif world > 1:
         run_ours_multi(args, rank, world, local_rank)
