@@ -340,10 +340,11 @@ def l2_plan(in_bytes, device):
                       f"steps (a {mib(2 * l2)} write, then a read of it, outside each step's events)")
 
 
-def time_steps_flushed(fn, steps, stream, l2_bytes):
+def time_steps_flushed(fn, steps, stream, l2_bytes, align=None):
     """ms per step with L2 flushed before every step: a write of twice L2 on `stream`, then a read of the same
     buffer (so L2 is left holding clean lines and the step pays for no write-back of the flush), then the step
-    between its own pair of events; the steps' event times are summed."""
+    between its own pair of events; the steps' event times are summed. `align` (N > 1: a device barrier of the
+    ranks) runs after the flush, outside the events, so a rank's step does not time the other ranks' flushes."""
     scratch = torch.empty(2 * l2_bytes // 4, dtype=torch.float32, device=stream.device)
     sink = torch.empty((), dtype=torch.float32, device=stream.device)
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
@@ -352,6 +353,8 @@ def time_steps_flushed(fn, steps, stream, l2_bytes):
         for i, (a, b) in enumerate(pairs):
             scratch.fill_(float(i))
             torch.amax(scratch, dim=0, out=sink)
+            if align is not None:
+                align()
             a.record(stream)
             fn()
             b.record(stream)
@@ -898,6 +901,8 @@ def run_ours_multi(args, rank, world, local_rank):
         step()
     torch.cuda.synchronize()
     flush, l2_bytes, l2_note = l2_plan(in_numel * es, dev)
+    if flush:
+        l2_note += "; then the ranks meet in a device barrier (dt_barrier, untimed) before each step's start event"
     nvl = NvLinkCounter(local_rank)
     l0 = capi.launch_count()
     with ClockSampler(local_rank) as clk:
@@ -905,9 +910,10 @@ def run_ours_multi(args, rank, world, local_rank):
         dist.barrier()
         torch.cuda.synchronize()
         c0 = nvl.read()
-        ms = (time_steps_flushed(step, args.steps, stream, l2_bytes) if flush
+        ms = (time_steps_flushed(step, args.steps, stream, l2_bytes,
+                                 align=lambda: comm.barrier(rank, stream.cuda_stream)) if flush
               else time_steps(step, args.steps, stream))
-    launches = capi.launch_count() - l0
+    launches = capi.launch_count() - l0 - (args.steps if flush else 0)  # the aligning barriers are untimed
     time.sleep(0.05)
     c1 = nvl.read()
     dist.barrier()
