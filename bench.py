@@ -329,10 +329,11 @@ def time_steps(fn, steps, stream):
     return start.elapsed_time(end) / steps  # ms per step
 
 
-def l2_plan(in_bytes, device):
+def l2_plan(in_bytes, device, l2_bytes=None):
     """How the timed steps keep L2 from serving the inputs: (flush, l2 bytes, description). Inputs larger than
-    L2 are not flushed; smaller ones get an L2 flush between timed steps (time_steps_flushed)."""
-    l2 = int(torch.cuda.get_device_properties(device).L2_cache_size)
+    L2 are not flushed; smaller ones get an L2 flush between timed steps (time_steps_flushed). `l2_bytes`
+    defaults to the device's L2 size."""
+    l2 = int(l2_bytes if l2_bytes is not None else torch.cuda.get_device_properties(device).L2_cache_size)
     mib = lambda b: f"{b / 2**20:.0f} MiB"  # noqa: E731
     if in_bytes > l2:
         return False, l2, f"inputs on this GPU ({mib(in_bytes)}) larger than L2 ({mib(l2)}); no flush"
